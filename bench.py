@@ -1,0 +1,590 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+Headline (BASELINE.json metric, configs[1]): causal prefill attention TFLOP/s at 2048
+positions, 17 heads x 128, bf16.  One step = the fused RoPE + QK-norm + KV-append pass over
+Q/K/V followed by the tcgen05 prefill attention kernel, i.e. the whole per-layer attention
+path of src/model.cpp:119-136 for a 2048-token prompt.  With N GPUs every rank prefills its
+own independent sequence (weak scaling, no collective on the data path).
+
+Also reported on the same line ("extra"): decode HBM GB/s for cfg1 (1 sequence, 512 keys) and
+cfg3 (64 sequences, kv_len ~ U[1,2048], sharded over ranks), and chunked-prefill TFLOP/s for
+cfg4 (4 sequences x 512 queries at offset 1536, sharded over ranks).
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching
+stream; L2 is flushed (a 256 MiB write) and the step's in-place input restored before every
+step, outside the events.  Barrier + synchronize on both sides of the timed loop; the max over
+ranks is reported.  `e2e` repeats the headline through the public API from pinned host
+buffers with the host->device copies of Q/K/V and the device->host copy of the output inside
+the timed region.
+
+--impl reference runs the same workloads through the reference's own CUDA kernels
+(kernels/rope.cu + kernels/flash_attention.cu rebuilt for sm_100a, oracle/_ref) and the
+reference's call sequence (two apply_rope_rmsnorm launches, two append copies,
+flash_attention per sequence).
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from nanochat_inferonly_lightning_b200 import workloads as W  # noqa: E402
+
+H, D, ROW = W.HEADS, W.HEAD_DIM, W.ROW
+FLUSH_BYTES = 256 << 20
+
+
+# ------------------------------------------------------------------------------ plumbing
+class Dist:
+    def __init__(self, n_gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != n_gpus:
+            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
+        torch.cuda.set_device(self.local)
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if not self.pg:
+            return x
+        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Single:
+    """A one-rank stand-in for Dist (reference arm)."""
+
+    def __init__(self, local):
+        self.rank, self.world, self.local = 0, 1, local
+
+    def barrier(self):
+        pass
+
+    def max(self, x):
+        return x
+
+    def sum(self, x):
+        return x
+
+    def close(self):
+        pass
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return {"hbm": j["hbm_gbs"], "tflops": j["bf16_tflops"], "src": "measured"}
+    return {"hbm": 6650.0, "tflops": 1590.0, "src": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernels from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except ValueError:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while a region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Stepper:
+    """Runs W warm-up and K timed steps; each step may record sub-events (kernel splits)."""
+
+    def __init__(self, dist, flush):
+        self.dist = dist
+        self.flush = flush
+
+    def run(self, step, K, Wm, restore=None, marks=0):
+        for _ in range(Wm):
+            if restore:
+                restore()
+            self.flush.zero_()
+            step([])
+        torch.cuda.synchronize()
+        self.dist.barrier()
+        torch.cuda.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(marks + 2)] for _ in range(K)]
+        for i in range(K):
+            if restore:
+                restore()
+            self.flush.zero_()
+            evs[i][0].record()
+            step(evs[i][1:-1])
+            evs[i][-1].record()
+        torch.cuda.synchronize()
+        self.dist.barrier()
+        torch.cuda.synchronize()
+        step_ms = [e[0].elapsed_time(e[-1]) for e in evs]
+        parts = [[e[j].elapsed_time(e[j + 1]) for e in evs] for j in range(marks + 1)]
+        return step_ms, parts
+
+
+# ------------------------------------------------------------------------------ workloads
+def prep_normed(impl, x, start_pos):
+    """RoPE + QK-norm in place (input setup, untimed) with the arm's own kernel, so the
+    reference arm never loads the product library."""
+    if impl.kind == "nc":
+        impl.nc.apply_rope_rmsnorm(x, x.shape[0], H, start_pos)
+    else:
+        assert impl.ref.ref_apply_rope_rmsnorm(ptr(x), x.shape[0], H, start_pos, stream()) == 0
+
+
+class Impl:
+    """The product path (nc_*) or the reference kernels (ref_*), same call shapes."""
+
+    def __init__(self, kind):
+        self.kind = kind
+        if kind == "nc":
+            import nanochat_inferonly_lightning_b200 as nc
+
+            self.nc = nc
+            self.lib = nc.load()
+            nc.init_rope_tables()
+        else:
+            import oracle
+
+            self.ref = oracle.reference_kernels()
+            if self.ref is None:
+                raise RuntimeError("reference kernels not built (oracle/_ref)")
+            assert self.ref.ref_init_rope_tables() == 0
+
+    # one layer's attention for one sequence chunk: RoPE+QK-norm(q,k), append, attention
+    def prefill_step(self, out, q, k, v, kc, vc, seq, start, ev=None):
+        if self.kind == "nc":
+            st = self.lib.nc_rope_qknorm_append(ptr(q), ptr(k), ptr(v), ptr(kc), ptr(vc), seq, H,
+                                                start, stream())
+            assert st == 0, st
+            if ev:
+                ev[0].record()
+            st = self.lib.nc_flash_attention(ptr(out), ptr(q), ptr(kc), ptr(vc), seq, start + seq,
+                                             H, W.SCALE, start, stream())
+            assert st == 0, st
+            return 2
+        r = self.ref
+        assert r.ref_apply_rope_rmsnorm(ptr(q), seq, H, start, stream()) == 0
+        assert r.ref_apply_rope_rmsnorm(ptr(k), seq, H, start, stream()) == 0
+        kc[start:start + seq].copy_(k[:seq])
+        vc[start:start + seq].copy_(v[:seq])
+        if ev:
+            ev[0].record()
+        assert r.ref_flash_attention(ptr(out), ptr(q), ptr(kc), ptr(vc), seq, start + seq, H,
+                                     float(W.SCALE), start, stream()) == 0
+        return 3
+
+
+def bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic, e2e=True):
+    q0, k0, v0 = (t.cuda() for t in W.cfg2_inputs(seed=1 + dist.rank))
+    S = W.CFG2_SEQ
+    q, k, v = q0.clone(), k0.clone(), v0.clone()
+    kc = torch.zeros((S, H, D), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.empty((S, ROW), dtype=torch.bfloat16, device="cuda")
+
+    def restore():
+        q.copy_(q0)
+        k.copy_(k0)
+
+    launches = [0]
+
+    def step(ev):
+        launches[0] += impl.prefill_step(out, q, k, v, kc, vc, S, 0, ev)
+
+    step_ms, parts = stepper.run(step, K, Wm, restore, marks=1)
+    launches_timed = (launches[0] // (K + Wm)) * K if impl.kind == "nc" else 0
+    t_step = dist.max(sum(step_ms) / K)
+    t_attn = dist.max(sum(parts[1]) / K)
+    flops_rank = W.CFG2_FLOPS
+    total = dist.sum(flops_rank)
+    res = {
+        "value": total / (t_step * 1e-3) / 1e12,
+        "ms_per_step": t_step,
+        "attn_kernel_ms": t_attn,
+        "prologue_ms": dist.max(sum(parts[0]) / K),
+        "gpu_launches": launches_timed,
+        "roofline": {
+            "bound": "tensor", "achieved": flops_rank / (t_attn * 1e-3) / 1e12,
+            "peak": peaks["tflops"], "unit": "TFLOP/s",
+            "frac": flops_rank / (t_attn * 1e-3) / 1e12 / peaks["tflops"],
+            "traffic": traffic.get("prefill_kernel_cfg2"),
+            "kernel": "prefill_kernel (tcgen05)" if impl.kind == "nc" else "flash_attention_kernel",
+            "peak_src": peaks["src"] + " bf16 burst",
+        },
+    }
+    if e2e:
+        res["e2e"] = bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0, kc, vc, out)
+    return res
+
+
+def bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0, kc, vc, out):
+    """Same step through the public API from pinned host buffers: H2D of Q/K/V, the attention
+    path, D2H of the output, all inside the timed region."""
+    S = W.CFG2_SEQ
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q0, k0, v0))
+    hout = torch.empty((S, ROW), dtype=torch.bfloat16).pin_memory()
+    q = torch.empty_like(q0)
+    k = torch.empty_like(k0)
+    v = torch.empty_like(v0)
+
+    def step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        impl.prefill_step(out, q, k, v, kc, vc, S, 0)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(Wm):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(K):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = dist.max(s.elapsed_time(e) / K)
+    bi = 3 * S * ROW * 2
+    bo = S * ROW * 2
+    return {"value": dist.sum(W.CFG2_FLOPS) / (t * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": t, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+
+
+def build_decode_batch(impl, lens, seed):
+    """Per-sequence caches [L_i, 17, 128] (rows 0..L_i-2 filled, normalised), plus the new
+    token's q/k/v [B, 17, 128] (pre-RoPE)."""
+    B = len(lens)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kcs, vcs = [], []
+    for L in lens:
+        kc = torch.randn((L, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+        vc = torch.randn((L, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+        prep_normed(impl, kc, 0)
+        kcs.append(kc)
+        vcs.append(vc)
+    q = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+    kn = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+    vn = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+    return q, kn, vn, kcs, vcs
+
+
+def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
+    a, b = W.shard(len(lens_all), dist.rank, dist.world)
+    lens = lens_all[a:b]
+    bytes_rank = W.decode_bytes(lens) if lens else 0
+    t_ms = 0.0
+    launches = 0
+    if lens:
+        q, kn, vn, kcs, vcs = build_decode_batch(impl, lens, seed=2 + dist.rank)
+        B = len(lens)
+        out = torch.empty((B, ROW), dtype=torch.bfloat16, device="cuda")
+        if impl.kind == "nc":
+            kp = torch.tensor([t.data_ptr() for t in kcs], dtype=torch.int64, device="cuda")
+            vp = torch.tensor([t.data_ptr() for t in vcs], dtype=torch.int64, device="cuda")
+            lt = torch.tensor(lens, dtype=torch.int32, device="cuda")
+            mx = max(lens)
+            ws = torch.zeros(impl.nc.decode_workspace_bytes(B, mx, H), dtype=torch.uint8,
+                             device="cuda")
+            lib = impl.lib
+
+            def step(ev):
+                st = lib.nc_decode_attention(ptr(out), ptr(q), ptr(kn), ptr(vn), ptr(kp), ptr(vp),
+                                             ptr(lt), B, H, W.SCALE, mx, 0, ptr(ws), ws.numel(),
+                                             stream())
+                assert st == 0, st
+
+            launches = 1
+        else:
+            r = impl.ref
+            qs = q.clone()
+            ks = kn.clone()
+
+            def step(ev):
+                qs.copy_(q)
+                ks.copy_(kn)
+                for i, L in enumerate(lens):
+                    qi = qs[i:i + 1]
+                    ki = ks[i:i + 1]
+                    assert r.ref_apply_rope_rmsnorm(ptr(qi), 1, H, L - 1, stream()) == 0
+                    assert r.ref_apply_rope_rmsnorm(ptr(ki), 1, H, L - 1, stream()) == 0
+                    kcs[i][L - 1:L].copy_(ki)
+                    vcs[i][L - 1:L].copy_(vn[i:i + 1])
+                    assert r.ref_flash_attention(ptr(out[i:i + 1]), ptr(qi), ptr(kcs[i]),
+                                                 ptr(vcs[i]), 1, L, H, float(W.SCALE), L - 1,
+                                                 stream()) == 0
+
+        step_ms, _ = stepper.run(step, K, Wm)
+        t_ms = sum(step_ms) / K
+    else:
+        stepper.run(lambda ev: None, K, Wm)
+    t = dist.max(t_ms)
+    total = dist.sum(bytes_rank)
+    gbs = total / (t * 1e-3) / 1e9 if t > 0 else 0.0
+    rank_gbs = bytes_rank / (t_ms * 1e-3) / 1e9 if t_ms > 0 else 0.0
+    return {
+        "value": gbs, "unit": "GB/s", "ms_per_step": t, "sequences": len(lens_all),
+        "bytes": W.decode_bytes(lens_all), "gpu_launches_per_step": launches,
+        "roofline": {"bound": "hbm", "achieved": rank_gbs, "peak": peaks["hbm"], "unit": "GB/s",
+                     "frac": rank_gbs / peaks["hbm"], "traffic": traffic.get(f"decode_kernel_{name}"),
+                     "peak_src": peaks["src"]},
+    }
+
+
+def bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic):
+    a, b = W.shard(W.CFG4_BATCH, dist.rank, dist.world)
+    n = b - a
+    off, C = W.CFG4_OFFSET, W.CFG4_CHUNK
+    t_ms = 0.0
+    if n > 0:
+        q0, k0, v0 = (t[a:b].cuda() for t in W.cfg4_chunk_inputs())
+        q, k = q0.clone(), k0.clone()
+        rows = off + C
+        g = torch.Generator(device="cuda").manual_seed(30 + dist.rank)
+        kslab = torch.randn((n, rows, H, D), generator=g, device="cuda").to(torch.bfloat16)
+        vslab = torch.randn((n, rows, H, D), generator=g, device="cuda").to(torch.bfloat16)
+        for i in range(n):
+            prep_normed(impl, kslab[i, :off], 0)
+        out = torch.empty((n, C, ROW), dtype=torch.bfloat16, device="cuda")
+
+        def restore():
+            q.copy_(q0)
+            k.copy_(k0)
+
+        if impl.kind == "nc":
+            lib = impl.lib
+            offs = torch.full((n,), off, dtype=torch.int32, device="cuda")
+
+            def step(ev):
+                for i in range(n):
+                    st = lib.nc_rope_qknorm_append(ptr(q[i]), ptr(k[i]), ptr(v0[i]), ptr(kslab[i]),
+                                                   ptr(vslab[i]), C, H, off, stream())
+                    assert st == 0, st
+                st = lib.nc_prefill_attention_batched(ptr(out), ptr(q), ptr(kslab), ptr(vslab),
+                                                      rows * ROW, rows, ptr(offs), n, C, H,
+                                                      W.SCALE, stream())
+                assert st == 0, st
+        else:
+            def step(ev):
+                for i in range(n):
+                    impl.prefill_step(out[i], q[i], k[i], v0[i], kslab[i], vslab[i], C, off)
+
+        step_ms, _ = stepper.run(step, K, Wm, restore)
+        t_ms = sum(step_ms) / K
+    else:
+        stepper.run(lambda ev: None, K, Wm)
+    t = dist.max(t_ms)
+    flops_rank = n * W.causal_flops(C, off)
+    total = dist.sum(flops_rank)
+    return {"value": total / (t * 1e-3) / 1e12 if t > 0 else 0.0, "unit": "TFLOP/s",
+            "ms_per_step": t, "sequences": W.CFG4_BATCH}
+
+
+def cpu_baseline_prefill(seconds_hint=20.0):
+    """The C oracle (fp32, OpenMP over rows) on a bounded sample of cfg2: the last `rows`
+    query rows of the 2048-position causal prefill (the most expensive rows), all 17 heads."""
+    import oracle
+
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    q, k, v = W.cfg2_inputs()
+    qu = q.view(torch.int16).numpy().view(np.uint16)
+    ku = k.view(torch.int16).numpy().view(np.uint16)
+    vu = v.view(torch.int16).numpy().view(np.uint16)
+    rows = 32
+    t0 = time.perf_counter()
+    oracle.flash_attention(qu[-rows:], ku, vu, rows, 2048, H, W.SCALE, 2048 - rows)
+    dt = time.perf_counter() - t0
+    # grow the sample toward ~seconds_hint of CPU work (bounded)
+    if dt < seconds_hint / 4:
+        rows = int(min(2048, max(rows, rows * (seconds_hint / 2) / max(dt, 1e-3))))
+        t0 = time.perf_counter()
+        oracle.flash_attention(qu[-rows:], ku, vu, rows, 2048, H, W.SCALE, 2048 - rows)
+        dt = time.perf_counter() - t0
+    flops = 2 * 2 * H * D * sum(2048 - rows + i + 1 for i in range(rows))
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"oracle/nc_oracle.c attention, last {rows} query rows of cfg2 "
+                      f"(17 heads, causal over 2048 keys), {dt:.1f} s"}
+
+
+# ------------------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["nc", "reference"], default="nc")
+    ap.add_argument("--no-extra", action="store_true", help="headline only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    args = ap.parse_args()
+    K, Wm = args.steps, max(args.warmup, 3)
+
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        # Rank 0 alone runs the reference arm; the other ranks leave without work.
+        rank = dist.rank
+        dist.close()
+        if rank != 0:
+            return
+        dist = Single(dist.local)
+    impl = Impl("nc" if args.impl == "nc" else "reference")
+    peaks = load_peaks()
+    traffic = load_traffic()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stepper = Stepper(dist, flush)
+
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    head = bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic)
+    extra = {}
+    if not args.no_extra:
+        extra["cfg1_decode"] = bench_decode(impl, dist, stepper, K, Wm, peaks, traffic,
+                                            [W.CFG1_LEN] if dist.rank == 0 else [], "cfg1") \
+            if dist.world == 1 else None
+        extra["cfg3_decode"] = bench_decode(impl, dist, stepper, K, Wm, peaks, traffic,
+                                            W.cfg3_kv_lens(), "cfg3")
+        extra["cfg4_chunked_prefill"] = bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic)
+    clk = clocks.stop()
+
+    line = {
+        "metric": "prefill attn TFLOP/s @2048 causal",
+        "value": head["value"],
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": K,
+        "warmup": Wm,
+        "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V at the BASELINE shapes)",
+        "config": {
+            "workload": "cfg2: causal prefill, 1 sequence x 2048 positions per GPU, 17 heads x 128;"
+                        " step = fused RoPE+QK-norm+KV-append pass + prefill attention",
+            "seq_len": W.CFG2_SEQ, "heads": H, "head_dim": D, "sequences_per_gpu": 1,
+            "l2": "flushed before every timed step (256 MiB write); inputs restored outside the events",
+            "parallelism": f"replica x{args.gpus} (independent sequences, no collective)",
+        },
+        "attn_kernel_ms": head["attn_kernel_ms"],
+        "prologue_ms": head["prologue_ms"],
+        "roofline": head["roofline"],
+        "e2e": head["e2e"],
+        "gpu_launches": head["gpu_launches"],
+        "clocks": clk,
+        "extra": extra,
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+        line["gpu_launches"] = 0
+        line["reference_kind"] = ("the reference's own CUDA kernels (kernels/rope.cu, "
+                                  "kernels/flash_attention.cu) rebuilt for sm_100a, called in "
+                                  "the reference's order; the reference has no CPU path")
+        line["cpu_baseline"] = {"value": head["value"], "unit": "TFLOP/s", "cores": 0,
+                                "kind": "reference",
+                                "sample": "full cfg2 on one B200 through the reference kernels"}
+    elif dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline_prefill()
+    if impl.kind == "nc":
+        st = impl.nc.device_status(reset=True)
+        line["device_status"] = st
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,162 @@
+/*
+ * nanochat_attn.h - C ABI of the B200 (sm_100a) attention hot path for the nanochat
+ * inference engine: RoPE / fused RoPE + QK-RMSNorm, KV-cache append, causal prefill
+ * attention on tcgen05 tensor cores, and split-KV decode attention.
+ *
+ * Library: libnanochat_attn_sm100.so.  Every function returns an nc_status (0 = success)
+ * and is asynchronous on the given stream unless stated otherwise.  All device pointers must
+ * be 16-byte aligned (cudaMalloc gives 256).  Tensors are bf16 (passed as void*), row-major:
+ *   Q, K, V, caches : [rows, heads, 128]      (head_dim is fixed at 128)
+ *   attention out   : [rows, heads * 128]
+ * The same library also exports the reference engine's own C++ entry points
+ * (namespace nanochat, see nanochat_attn_dropin.hpp), so it links in place of the
+ * reference's kernels/flash_attention.cu and kernels/rope.cu.
+ */
+#ifndef NANOCHAT_ATTN_H
+#define NANOCHAT_ATTN_H
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nc_status {
+    NC_OK = 0,
+    NC_ERR_INVALID_ARG = 1,     /* bad size, null pointer, heads outside [1, 32] ...      */
+    NC_ERR_MISALIGNED = 2,      /* a pointer is not 16-byte aligned                        */
+    NC_ERR_CUDA = 3,            /* a CUDA runtime call failed (see nc_last_cuda_error)     */
+    NC_ERR_WORKSPACE = 4,       /* workspace missing or smaller than required              */
+    NC_ERR_RANGE = 5,           /* a position is beyond the RoPE table (20480 positions)   */
+    NC_ERR_DEVICE_TIMEOUT = 6   /* a kernel's bounded wait gave up (nc_device_status)      */
+} nc_status;
+
+/* Human-readable name of a status code. */
+const char* nc_status_string(int status);
+/* The last cudaError_t seen by this thread (0 if none). */
+int nc_last_cuda_error(void);
+/* Status of the most recent call made through the void-returning nanochat:: entry points
+ * on this thread (those cannot return it). */
+int nc_last_status(void);
+/* Reads (and, if reset != 0, clears) the current device's kernel status word.  Non-zero
+ * means a kernel's bounded wait gave up; bits 0x100 | tag identify the wait.  Synchronous. */
+int nc_device_status(int reset);
+
+/* Builds the fp32 cos/sin table (positions 0..20479, base 10000, 64 frequencies) on the
+ * host with the reference's expression order and uploads it to the current device.
+ * Synchronous.  Other entry points upload it on first use per device, so calling this is
+ * optional; call it before any stream capture.
+ * Replaces: kernels/rope.cu:14-30 (init_rope_tables), declared src/model.h:16. */
+int nc_init_rope_tables(void);
+
+/* In place: half-split RoPE at positions start_pos.. with one bf16 rounding.
+ * Replaces: kernels/rope.cu:34-68 (apply_rope), declared src/model.h:14. */
+int nc_apply_rope(void* x, int seq_len, int n_heads, int start_pos, cudaStream_t stream);
+
+/* In place: RoPE then parameter-free RMSNorm per head (eps 1e-6), one bf16 rounding.
+ * Replaces: kernels/rope.cu:74-158 (apply_rope_rmsnorm), declared src/model.h:15. */
+int nc_apply_rope_rmsnorm(void* x, int seq_len, int n_heads, int start_pos,
+                          cudaStream_t stream);
+
+/* Fused prologue of one attention layer: q gets RoPE + QK-norm in place; k gets RoPE +
+ * QK-norm and is written to k_cache rows [start_pos, start_pos + seq_len); v is copied to the
+ * same rows of v_cache.  k and v are not modified.
+ * Replaces: the two apply_rope_rmsnorm calls and the two cache-append cudaMemcpyAsync
+ * calls of Model::attention, src/model.cpp:119-131. */
+int nc_rope_qknorm_append(void* q, const void* k, const void* v, void* k_cache, void* v_cache,
+                          int seq_len, int heads, int start_pos, cudaStream_t stream);
+
+/* out[s, h, :] = softmax(scale * Q[s,h] . K[j,h]^T) V[j,h] over keys j < kv_len with
+ * j <= s + kv_offset; fp32 softmax, bf16 output.  seq_q > 1 runs the tcgen05 prefill
+ * kernel; seq_q == 1 runs the split-KV decode kernel (its partial results live in a
+ * per-device workspace the library allocates on first use and grows as needed).  A row with
+ * no visible key gets NaN, as the reference's 0/0 does.
+ * Replaces: kernels/flash_attention.cu:159-171 (flash_attention), declared src/model.h:26-27;
+ * called from src/model.cpp:134-136. */
+int nc_flash_attention(void* out, const void* Q, const void* K, const void* V, int seq_q,
+                       int kv_len, int heads, float scale, int kv_offset, cudaStream_t stream);
+
+/* Bytes of workspace nc_decode_attention needs for this batch and bound on kv_len. */
+size_t nc_decode_workspace_bytes(int batch, int max_kv_len, int heads, int split_len);
+
+/* Batched decode step for `batch` independent sequences, one query token each.
+ *   q       [batch, heads, 128]: the new tokens' queries.  If k_new/v_new are non-null, q
+ *           is taken before RoPE and gets RoPE + QK-norm inside the kernel (q is not
+ *           written); the new key gets RoPE + QK-norm and, with the value, is appended at
+ *           row kv_len[b]-1 of sequence b's cache.  If k_new/v_new are null, q is used as
+ *           given and the caches must already hold rows [0, kv_len[b]).
+ *   k_caches, v_caches  device arrays [batch] of per-sequence cache bases ([rows,heads,128])
+ *   kv_len  device array [batch]: keys visible to sequence b (its query sits at position
+ *           kv_len[b]-1), 1 <= kv_len[b] <= max_kv_len.
+ *   split_len  keys per split-KV chunk (multiple of 16) or 0 for automatic.
+ *   workspace  >= nc_decode_workspace_bytes(...) bytes, zero-filled before first use; the
+ *           kernel leaves it ready for the next call (calls sharing one workspace must not
+ *           overlap on the GPU).
+ * Replaces: the seq_len == 1 path of Model::attention (src/model.cpp:119-136): two
+ * apply_rope_rmsnorm launches, two append copies and flash_attention, for one sequence. */
+int nc_decode_attention(void* out, const void* q, const void* k_new, const void* v_new,
+                        void* const* k_caches, void* const* v_caches, const int* kv_len,
+                        int batch, int heads, float scale, int max_kv_len, int split_len,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Batched causal prefill (chunked, with cache offset) for `batch` sequences whose caches
+ * are slices of one slab: sequence b's rows start at k_slab + b * seq_stride elements
+ * (seq_stride >= rows_per_seq * heads * 128).  Sequence b's chunk of seq_q queries sits at
+ * positions kv_offset[b] .. kv_offset[b] + seq_q - 1 and its keys [0, kv_offset[b] + seq_q)
+ * must already be in the cache (see nc_rope_qknorm_append).
+ *   q   [batch, seq_q, heads, 128] (after RoPE + QK-norm), out [batch, seq_q, heads*128].
+ *   kv_offset  device array [batch].
+ * Replaces: per-sequence flash_attention(seq_q, kv_len, kv_offset) calls of
+ * src/model.cpp:134-136 for a chunk appended at start_pos = kv_offset. */
+int nc_prefill_attention_batched(void* out, const void* q, const void* k_slab,
+                                 const void* v_slab, long long seq_stride, int rows_per_seq,
+                                 const int* kv_offset, int batch, int seq_q, int heads,
+                                 float scale, cudaStream_t stream);
+
+/* ----------------------------------------------------------------------------------------
+ * KV cache.  One slab per layer and per K/V: [n_seqs][max_len][heads][128] bf16, allocated
+ * once at full length and zero-filled (no grow-and-copy), with per-sequence lengths tracked
+ * on the host and device arrays of per-sequence base pointers for the batched kernels.
+ * Replaces: struct KVCache (src/model.h:65-73) and KVCache::allocate/grow/clear
+ * (src/model.cpp:52-81), whose growth path reallocates and copies synchronously. */
+typedef struct nc_kv_cache nc_kv_cache;
+
+int nc_kv_cache_create(nc_kv_cache** out, int n_layers, int n_seqs, int max_len, int heads);
+int nc_kv_cache_destroy(nc_kv_cache* cache);
+/* Device base of sequence `seq` in layer `layer` (rows [0, max_len)). */
+void* nc_kv_cache_k(nc_kv_cache* cache, int layer, int seq);
+void* nc_kv_cache_v(nc_kv_cache* cache, int layer, int seq);
+/* Device arrays [n_seqs] of the per-sequence bases of one layer. */
+void* const* nc_kv_cache_k_table(nc_kv_cache* cache, int layer);
+void* const* nc_kv_cache_v_table(nc_kv_cache* cache, int layer);
+/* Elements between consecutive sequences of one slab. */
+long long nc_kv_cache_seq_stride(const nc_kv_cache* cache);
+int nc_kv_cache_max_len(const nc_kv_cache* cache);
+/* Host-side length bookkeeping: rows filled for (layer, seq), like KVCache::current_len. */
+int nc_kv_cache_len(const nc_kv_cache* cache, int layer, int seq);
+int nc_kv_cache_set_len(nc_kv_cache* cache, int layer, int seq, int len);
+/* Resets one sequence (seq >= 0) or all sequences (seq < 0) to length 0 in every layer,
+ * like KVCache::clear (src/model.h:72).  Contents are kept. */
+int nc_kv_cache_clear(nc_kv_cache* cache, int seq);
+
+/* Prefill one sequence's chunk through the cache: RoPE + QK-norm + append of k/v at the
+ * sequence's current length in `layer`, then causal attention of q over the cache; advances
+ * that length by seq_len.  q is modified in place (RoPE + QK-norm).  Mirrors the
+ * apply_rope_rmsnorm -> append -> flash_attention sequence of src/model.cpp:119-136. */
+int nc_kv_cache_prefill(nc_kv_cache* cache, int layer, int seq, void* out, void* q,
+                        const void* k, const void* v, int seq_len, float scale,
+                        cudaStream_t stream);
+
+/* One decode step for every sequence of the cache in `layer`: q/k_new/v_new are
+ * [n_seqs, heads, 128] before RoPE; the new keys/values are appended at each sequence's
+ * current length, which then advances by one.  Uses a workspace owned by the cache, so
+ * calls on one cache must be ordered on one stream. */
+int nc_kv_cache_decode(nc_kv_cache* cache, int layer, void* out, const void* q,
+                       const void* k_new, const void* v_new, float scale, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NANOCHAT_ATTN_H */

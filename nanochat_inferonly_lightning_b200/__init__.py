@@ -1,0 +1,16 @@
+"""B200-native (sm_100a) attention hot path of the nanochat inference engine.
+
+The compute lives in libnanochat_attn_sm100.so (CUDA kernels + C ABI, include/nanochat_attn.h);
+this package is the Python-side mirror of the reference's entry points over that ABI.
+Importing it does not load the library; the first call does, and raises if it is missing.
+"""
+from ._lib import LIB_PATH, NcError, load
+from .attn import (HEAD_DIM, ROPE_MAX_SEQ, KVCache, apply_rope, apply_rope_rmsnorm,
+                   decode_attention, decode_workspace_bytes, device_status, flash_attention,
+                   init_rope_tables, prefill_attention_batched, rope_qknorm_append)
+
+__all__ = [
+    "LIB_PATH", "NcError", "load", "HEAD_DIM", "ROPE_MAX_SEQ", "KVCache", "apply_rope",
+    "apply_rope_rmsnorm", "decode_attention", "decode_workspace_bytes", "device_status",
+    "flash_attention", "init_rope_tables", "prefill_attention_batched", "rope_qknorm_append",
+]

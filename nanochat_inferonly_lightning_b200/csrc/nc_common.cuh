@@ -1,0 +1,178 @@
+// Shared device helpers and the launch entry points that the host API layer calls.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace nc {
+
+// Model geometry fixed by the reference engine (src/config.h:12, :17).
+constexpr int kHeadDim = 128;
+constexpr int kHalfDim = kHeadDim / 2;
+constexpr int kRopeMaxSeq = 2048 * 10;  // positions covered by the cos/sin table
+constexpr float kRopeBase = 10000.0f;
+constexpr float kNormEps = 1e-6f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+using bf16 = __nv_bfloat16;
+
+// ---------------------------------------------------------------------------------------
+// small device utilities
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
+    uint4 r;
+    r.x = pack_bf16x2(f[0], f[1]);
+    r.y = pack_bf16x2(f[2], f[3]);
+    r.z = pack_bf16x2(f[4], f[5]);
+    r.w = pack_bf16x2(f[6], f[7]);
+    return r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// RoPE (+ optional parameter-free RMSNorm) of one 128-wide head row held by a half-warp:
+// lane `sub` (0..15) owns dims [8*sub, 8*sub+8).  Half-split pairing (dim i with i+64,
+// reference kernels/rope.cu:95-97) puts a lane's partner at sub^8.  `mask` is the
+// half-warp's shuffle mask.  Rotation: y0 = x0*c + x1*s, y1 = x1*c - x0*s
+// (kernels/rope.cu:105-107); the norm is y * rsqrt(mean(y^2) + 1e-6) (kernels/rope.cu:137).
+// `cs` is the interleaved cos/sin table: cs[pos * 64 + i] = (cos(pos*f_i), sin(pos*f_i)).
+__device__ __forceinline__ void rope_norm_row(const float2* __restrict__ cs_table,
+                                              const uint4 raw, int sub, unsigned mask, int pos,
+                                              bool norm, float (&y)[8]) {
+    uint4 pr;
+    pr.x = __shfl_xor_sync(mask, raw.x, 8);
+    pr.y = __shfl_xor_sync(mask, raw.y, 8);
+    pr.z = __shfl_xor_sync(mask, raw.z, 8);
+    pr.w = __shfl_xor_sync(mask, raw.w, 8);
+    float xo[8], xp[8];
+    bf16x8_to_f32(raw, xo);
+    bf16x8_to_f32(pr, xp);
+    const float4* cs = reinterpret_cast<const float4*>(cs_table + (size_t)pos * kHalfDim +
+                                                       8 * (sub & 7));
+    float c[8], s[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 t = __ldg(cs + i);
+        c[2 * i] = t.x;
+        s[2 * i] = t.y;
+        c[2 * i + 1] = t.z;
+        s[2 * i + 1] = t.w;
+    }
+    if (sub < 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = __fmaf_rn(xo[e], c[e], xp[e] * s[e]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = __fmaf_rn(xo[e], c[e], -(xp[e] * s[e]));
+    }
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = __fmaf_rn(y[e], y[e], ss);
+        ss += __shfl_xor_sync(mask, ss, 8);
+        ss += __shfl_xor_sync(mask, ss, 4);
+        ss += __shfl_xor_sync(mask, ss, 2);
+        ss += __shfl_xor_sync(mask, ss, 1);
+        const float r = rsqrtf(ss * (1.0f / kHeadDim) + kNormEps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] *= r;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// launch entry points (defined in rope.cu / decode.cu / prefill.cu)
+// ---------------------------------------------------------------------------------------
+enum RopeMode : int { kRopeOnly = 0, kRopeNorm = 1, kRopeNormAppend = 2 };
+
+struct RopeArgs {
+    const float2* rope_cs;  // device cos/sin table
+    bf16* q;              // [rows, heads, 128]; modified in place
+    const bf16* k;        // append mode: [rows, heads, 128] pre-RoPE keys
+    const bf16* v;        // append mode: [rows, heads, 128] values
+    bf16* k_dst;          // append mode: destination rows (cache row start_pos)
+    bf16* v_dst;
+    int seq_len;
+    int heads;
+    int start_pos;
+};
+
+cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream);
+// Uploads the table to the current device and returns its device address there.
+cudaError_t upload_rope_table(const float2** device_table);
+
+struct DecodeArgs {
+    const float2* rope_cs;        // device cos/sin table (fused RoPE only)
+    bf16* out;                    // [B, heads*128]
+    const bf16* q;                // [B, heads, 128]
+    const bf16* k_new;            // [B, heads, 128] pre-RoPE key of the new token, or null
+    const bf16* v_new;            // [B, heads, 128] value of the new token, or null
+    bf16* const* k_cache;         // device array [B] of per-sequence K bases, or null
+    bf16* const* v_cache;
+    bf16* k_single;               // single-sequence mode (B == 1): K base, used if k_cache null
+    bf16* v_single;
+    const int* kv_len;            // device [B] visible keys, or null (then n_visible_single)
+    int n_visible_single;
+    int max_kv_len;               // host bound on kv_len[b]; sized the grid and workspace
+    int batch;
+    int heads;
+    int q_raw;                    // 1: q is pre-RoPE and gets RoPE + QK-norm in the kernel
+    float scale_log2;             // softmax scale * log2(e)
+    int split_len;                // keys per split (multiple of 16)
+    int max_splits;
+    float* part_o;                // [B, max_splits, heads, 128]
+    float2* part_ml;              // [B, max_splits, heads]
+    unsigned* counters;           // [B], zero between launches
+    int* status;                  // device status word (argument violations seen on device)
+};
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
+size_t decode_workspace_bytes(int batch, int max_splits, int heads);
+
+struct PrefillArgs {
+    bf16* out;                    // [B, seq_q, heads*128]
+    const bf16* q;                // [B, seq_q, heads, 128]
+    const bf16* k;                // K rows of sequence b start at k + b*kv_batch_stride
+    const bf16* v;
+    long long kv_batch_stride;    // elements between sequences (0 when B == 1)
+    int kv_rows;                  // rows addressable per sequence (tensor-map extent)
+    const int* kv_offset_dev;     // device [B] offsets, or null (then kv_offset / kv_len)
+    int kv_offset;
+    int kv_len;
+    int batch;
+    int seq_q;
+    int heads;
+    float scale;
+    int* status;                  // device status word for bounded waits
+};
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+
+}  // namespace nc

@@ -1,0 +1,398 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05 + tensor memory),
+// with Q/K/V tiles staged in shared memory by TMA.
+//
+// Replaces the seq_q > 1 use of reference kernels/flash_attention.cu:19-171, which runs one
+// 128-thread CTA per (query, head) on CUDA cores and walks every key up to kv_len.
+//
+// Work unit: one CTA = 128 query rows x one head x one sequence.  Keys are consumed in
+// blocks of 128; only blocks that hold a visible key are visited (causal rule
+// key <= query + kv_offset and key < kv_len, reference flash_attention.cu:37, :74).
+//
+// Roles (192 threads):
+//   warp 0      TMA producer: Q tile once, then K(j), V(j) into single-buffered tiles.
+//   warp 1      allocates 256 TMEM columns; one lane issues every tcgen05.mma.
+//   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
+// Tensor memory: S = Q.K^T (fp32, columns [0,128)); P (bf16 pairs) overwrites S columns
+// [0,64) and feeds the P.V MMA straight from TMEM; O (fp32) in columns [128,256).
+// Per key block j:   QK(j) -> softmax(j) -> PV(j) -> QK(j+1) ...
+// Two CTAs share each SM (96 KB smem, 256 TMEM columns each), so one CTA's softmax runs
+// while the other's MMAs occupy the tensor pipe.
+//
+// Softmax: fp32, base-2 exponentials of scale*log2(e)-scaled scores, with a lazily updated
+// reference max: O and the row sum are rescaled only when a block's max exceeds the
+// reference by more than 8 (log2 units).  Rows without any visible key produce NaN, as the
+// reference's 0/0 does.
+#include <cuda.h>
+
+#include "nc_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace nc {
+
+namespace {
+
+constexpr int kBM = 128;             // query rows per CTA
+constexpr int kBN = 128;             // keys per block
+constexpr int kThreads = 192;
+constexpr uint32_t kBoxBytes = 64 * 128 * 2;    // one 64-dim x 128-row box, 128B swizzle
+constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 x 128 bf16
+constexpr uint32_t kTmemCols = 256;
+constexpr float kRescaleThreshold = 8.0f;
+constexpr float kNegInf = -__builtin_huge_valf();
+
+enum Bar : int {
+    kBarQ = 0,
+    kBarKFull,
+    kBarKFree,
+    kBarVFull,
+    kBarVFree,
+    kBarS,
+    kBarP,
+    kBarO,
+    kBarOFinal,
+    kNumBars
+};
+
+struct __align__(8) SmemTail {
+    uint64_t bars[kNumBars];
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 3 * kTileBytes + sizeof(SmemTail);
+
+struct PrefillKParams {
+    bf16* out;
+    const int* kv_offset_dev;
+    int kv_offset;
+    int kv_len;
+    int kv_len_from_offset;  // batched mode: kv_len_b = kv_offset_b + seq_q
+    int batch;
+    int seq_q;
+    int heads;
+    int n_qtiles;
+    float scale_log2;
+    int* status;
+};
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* tmap, uint64_t* bar,
+                                            int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const PrefillKParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kTileBytes;
+    uint8_t* sV = smem + 2 * kTileBytes;
+    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 3 * kTileBytes);
+    uint64_t* bars = tail->bars;
+    volatile int* abort_flag = &tail->abort;
+
+    // Longest-first tile order: consecutive block indices walk all (head, seq) groups of
+    // the last (longest) query tile first.
+    const int groups = p.heads * p.batch;
+    const int rank = blockIdx.x / groups;
+    const int g = blockIdx.x - rank * groups;
+    const int t = p.n_qtiles - 1 - rank;
+    const int h = g % p.heads;
+    const int b = g / p.heads;
+    const int q0 = t * kBM;
+    const int off = p.kv_offset_dev ? p.kv_offset_dev[b] : p.kv_offset;
+    const int kv_len = p.kv_len_from_offset ? off + p.seq_q : p.kv_len;
+    const int q_last = min(q0 + kBM - 1, p.seq_q - 1);
+    const int kv_end = min(kv_len, q_last + off + 1);  // keys [0, kv_end) may be visible
+    const int nb = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], i == kBarP ? 128u : 1u);
+        tail->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tail->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem_base;
+    const uint32_t tS = tmem;        // S (fp32) / P (bf16x2, first 64 columns)
+    const uint32_t tO = tmem + 128;  // O (fp32)
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ producer
+        if (lane == 0 && nb > 0) {
+            const int x0 = h * 128;
+            mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
+            tma_load_3d(sQ, &tmQ, &bars[kBarQ], x0, q0, b);
+            tma_load_3d(sQ + kBoxBytes, &tmQ, &bars[kBarQ], x0 + 64, q0, b);
+            for (int j = 0; j < nb; ++j) {
+                if (j > 0 && !mbar_wait(&bars[kBarKFree], (j - 1) & 1, abort_flag, p.status, 1)) break;
+                mbar_arrive_expect_tx(&bars[kBarKFull], kTileBytes);
+                tma_load_3d(sK, &tmK, &bars[kBarKFull], x0, j * kBN, b);
+                tma_load_3d(sK + kBoxBytes, &tmK, &bars[kBarKFull], x0 + 64, j * kBN, b);
+                if (j > 0 && !mbar_wait(&bars[kBarVFree], (j - 1) & 1, abort_flag, p.status, 2)) break;
+                mbar_arrive_expect_tx(&bars[kBarVFull], kTileBytes);
+                tma_load_3d(sV, &tmV, &bars[kBarVFull], x0, j * kBN, b);
+                tma_load_3d(sV + kBoxBytes, &tmV, &bars[kBarVFull], x0 + 64, j * kBN, b);
+            }
+            // Do not leave the CTA with loads still landing in shared memory.
+            mbar_wait(&bars[kBarVFree], (nb - 1) & 1, abort_flag, p.status, 3);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0 && nb > 0) {
+            const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
+            const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
+            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+            bool ok = mbar_wait(&bars[kBarQ], 0, abort_flag, p.status, 4);
+            for (int j = 0; ok && j < nb; ++j) {
+                if (!mbar_wait(&bars[kBarKFull], j & 1, abort_flag, p.status, 5)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t koff = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    mma_ss(tS, smem_desc_sw128(aQ + koff, 16, 1024),
+                           smem_desc_sw128(aK + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&bars[kBarKFree]);
+                mma_commit(&bars[kBarS]);
+                if (!mbar_wait(&bars[kBarP], j & 1, abort_flag, p.status, 6)) break;
+                if (!mbar_wait(&bars[kBarVFull], j & 1, abort_flag, p.status, 7)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    // 16 keys per MMA: P columns [8kk, 8kk+8) (bf16 pairs), V rows
+                    // [16kk, 16kk+16) = two 8-row swizzle groups.
+                    mma_ts(tO, tS + kk * 8, smem_desc_sw128(aV + kk * 2048, kBoxBytes, 1024),
+                           idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&bars[kBarVFree]);
+                if (j + 1 < nb) {
+                    // P aliases S: the next QK must not start before this PV has read P.
+                    mma_commit(&bars[kBarO]);
+                    if (!mbar_wait(&bars[kBarO], j & 1, abort_flag, p.status, 8)) break;
+                } else {
+                    mma_commit(&bars[kBarOFinal]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ softmax / epilogue
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int q = q0 + r;
+        const int qlim = q + off;  // last visible key for this row
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const float sl2 = p.scale_log2;
+        float m_ref = kNegInf, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nb; ++j) {
+            // Warp-uniform outcome: the TMEM loads below are warp-collective.
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarS], j & 1, abort_flag, p.status, 9))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[128];
+            {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t raw[32];
+                    tmem_ld32_sync(tS + lane_base + 32 * c, raw);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(raw[i]);
+                }
+            }
+            const int key0 = j * kBN;
+            if (key0 + kBN - 1 > q0 + off || key0 + kBN > kv_len) {
+#pragma unroll
+                for (int c = 0; c < 128; ++c) {
+                    const int key = key0 + c;
+                    if (key > qlim || key >= kv_len) s[c] = kNegInf;
+                }
+            }
+            float bm = s[0];
+#pragma unroll
+            for (int c = 1; c < 128; ++c) bm = fmaxf(bm, s[c]);
+            const float bm2 = bm * sl2;
+            const bool renew = (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
+            float alpha = 1.f;
+            if (renew) {
+                alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
+                m_ref = bm2;
+            }
+            l *= alpha;
+            // O holds the sum through PV(j-1) and is idle now; rescale rows that renewed.
+            if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t raw[32];
+                    tmem_ld32_sync(tO + lane_base + 32 * c, raw);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
+                    tmem_st32_sync(tO + lane_base + 32 * c, raw);
+                }
+            }
+            const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
+            float rowsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t pk[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = fast_exp2(__fmaf_rn(s[64 * c + 2 * i], sl2, -mu));
+                    const float p1 = fast_exp2(__fmaf_rn(s[64 * c + 2 * i + 1], sl2, -mu));
+                    rowsum += p0 + p1;
+                    pk[i] = pack_bf16x2(p0, p1);
+                }
+                tmem_st32_sync(tS + lane_base + 32 * c, pk);
+            }
+            l += rowsum;
+            tc_fence_before();
+            mbar_arrive(&bars[kBarP]);
+        }
+        // Epilogue: O / l -> bf16 -> out[b, q, h, :].
+        bf16* orow = p.out + (((size_t)b * p.seq_q + q) * p.heads + h) * kHeadDim;
+        const bool store = q < p.seq_q;
+        if (nb == 0) {
+            if (store) {
+                const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
+            }
+        } else if (ok && __all_sync(0xFFFFFFFFu,
+                                    mbar_wait(&bars[kBarOFinal], 0, abort_flag, p.status, 10))) {
+            tc_fence_after();
+            const float inv = 1.0f / l;  // l == 0 (no visible key) gives 0 * inf = NaN
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t raw[32];
+                tmem_ld32_sync(tO + lane_base + 32 * c, raw);
+                if (store) {
+                    uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint4 w;
+                        w.x = pack_bf16x2(__uint_as_float(raw[8 * i + 0]) * inv,
+                                          __uint_as_float(raw[8 * i + 1]) * inv);
+                        w.y = pack_bf16x2(__uint_as_float(raw[8 * i + 2]) * inv,
+                                          __uint_as_float(raw[8 * i + 3]) * inv);
+                        w.z = pack_bf16x2(__uint_as_float(raw[8 * i + 4]) * inv,
+                                          __uint_as_float(raw[8 * i + 5]) * inv);
+                        w.w = pack_bf16x2(__uint_as_float(raw[8 * i + 6]) * inv,
+                                          __uint_as_float(raw[8 * i + 7]) * inv);
+                        dst[i] = w;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side: tensor maps
+// ---------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 3-D map over [batch][rows][heads*128] bf16 with a (64 dims, 128 rows, 1) box, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
+              long long batch_stride_elems) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)heads * 128, (cuuint64_t)rows, (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)heads * 128 * 2,
+                                   (cuuint64_t)(batch > 1 ? batch_stride_elems * 2
+                                                          : (long long)rows * heads * 128 * 2)};
+    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
+    if (a.batch <= 0 || a.seq_q <= 0) return cudaSuccess;
+    // The shared-memory opt-in is per device context; remember it per device.
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return e0;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kSmemBytes);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const int kv_rows = a.kv_rows;
+    if (!make_map(&mq, a.q, a.heads, a.seq_q, a.batch, (long long)a.seq_q * a.heads * 128) ||
+        !make_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride) ||
+        !make_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride))
+        return cudaErrorInvalidValue;
+    PrefillKParams kp;
+    kp.out = a.out;
+    kp.kv_offset_dev = a.kv_offset_dev;
+    kp.kv_offset = a.kv_offset;
+    kp.kv_len = a.kv_len;
+    kp.kv_len_from_offset = a.kv_offset_dev != nullptr;
+    kp.batch = a.batch;
+    kp.seq_q = a.seq_q;
+    kp.heads = a.heads;
+    kp.n_qtiles = (a.seq_q + kBM - 1) / kBM;
+    kp.scale_log2 = a.scale * kLog2e;
+    kp.status = a.status;
+    const long long nblocks = (long long)kp.n_qtiles * a.heads * a.batch;
+    prefill_kernel<<<(unsigned)nblocks, kThreads, kSmemBytes, stream>>>(mq, mk, mv, kp);
+    return cudaGetLastError();
+}
+
+}  // namespace nc

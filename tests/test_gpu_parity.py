@@ -1,0 +1,345 @@
+"""GPU parity of the CUDA path (called through the C ABI) against the CPU oracle and against
+the reference's own kernels rebuilt for sm_100a.
+
+Tolerance for attention outputs (bf16): max-abs 2e-2 and mean-abs 2e-3; NaN positions equal.
+RoPE alone is bit-exact against the oracle (same fp32 table, same fused multiply-adds); RoPE +
+QK-norm may differ by one bf16 ulp where the GPU's rsqrt and the oracle's 1/sqrt round apart.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_close_bf16, bf16_to_u16, u16_to_bf16, ulp_diff_bf16
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+H = 17
+D = 128
+SCALE = 1.0 / np.sqrt(128.0)
+
+
+@pytest.fixture(scope="module")
+def nc():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import nanochat_inferonly_lightning_b200 as m
+
+    m.init_rope_tables()
+    yield m
+    torch.cuda.synchronize()
+    assert m.device_status(reset=True) == 0, "a kernel's bounded wait gave up"
+
+
+@pytest.fixture(scope="module")
+def ref():
+    lib = oracle.reference_kernels()
+    if lib is None:
+        pytest.skip("reference kernels not built (oracle/_ref)")
+    assert lib.ref_init_rope_tables() == 0
+    return lib
+
+
+def randn_u16(shape, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    t = (torch.randn(shape, generator=g, dtype=torch.float32) * scale).to(torch.bfloat16)
+    return bf16_to_u16(t)
+
+
+def normed(x_u16, start_pos=0):
+    """RoPE + QK-norm by the oracle (rows are positions start_pos..)."""
+    return oracle.apply_rope_rmsnorm(x_u16, x_u16.shape[0], x_u16.shape[1], start_pos)
+
+
+def dev(a_u16):
+    return u16_to_bf16(a_u16, "cuda")
+
+
+def stream_ptr():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def guarded(n_elems, guard=4096):
+    """A device buffer with poisoned guard regions before and after the payload."""
+    buf = torch.full((n_elems + 2 * guard,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    buf.view(torch.int16).fill_(0x5A5A)
+    return buf, buf[guard:guard + n_elems]
+
+
+def guards_intact(buf, guard=4096):
+    v = buf.view(torch.int16)
+    return bool((v[:guard] == 0x5A5A).all()) and bool((v[-guard:] == 0x5A5A).all())
+
+
+# ----------------------------------------------------------------------------- RoPE tables
+def test_reference_rope_table_matches_oracle(ref):
+    """Pins the oracle's table to the reference's own init_rope_tables (bit-exact)."""
+    n = 20480
+    c = np.zeros((n, 64), np.float32)
+    s = np.zeros((n, 64), np.float32)
+    assert ref.ref_get_rope_tables(c.ctypes.data_as(ctypes.c_void_p),
+                                   s.ctypes.data_as(ctypes.c_void_p), n) == 0
+    oc, os_ = oracle.rope_tables()
+    assert np.array_equal(c.view(np.uint32), oc.view(np.uint32))
+    assert np.array_equal(s.view(np.uint32), os_.view(np.uint32))
+
+
+# ----------------------------------------------------------------------------- RoPE
+@pytest.mark.parametrize("seq_len,start_pos", [(1, 0), (3, 511), (64, 1000), (129, 20480 - 129)])
+def test_apply_rope_bit_exact(nc, ref, seq_len, start_pos):
+    x = randn_u16((seq_len, H, D), 10 + seq_len)
+    want = oracle.apply_rope(x, seq_len, H, start_pos)
+    t = dev(x)
+    nc.apply_rope(t, seq_len, H, start_pos)
+    got = bf16_to_u16(t)
+    assert np.array_equal(got, want)
+    # the reference kernel agrees with the oracle to one bf16 ulp
+    r = dev(x)
+    assert ref.ref_apply_rope(ctypes.c_void_p(r.data_ptr()), seq_len, H, start_pos, stream_ptr()) == 0
+    torch.cuda.synchronize()
+    assert ulp_diff_bf16(bf16_to_u16(r), want).max() <= 1
+
+
+@pytest.mark.parametrize("seq_len,start_pos", [(1, 511), (7, 0), (128, 1536), (300, 17)])
+def test_apply_rope_rmsnorm(nc, ref, seq_len, start_pos):
+    x = randn_u16((seq_len, H, D), 20 + seq_len)
+    want = oracle.apply_rope_rmsnorm(x, seq_len, H, start_pos)
+    t = dev(x)
+    nc.apply_rope_rmsnorm(t, seq_len, H, start_pos)
+    got = bf16_to_u16(t)
+    d = ulp_diff_bf16(got, want)
+    assert d.max() <= 1 and (d == 0).mean() >= 0.99
+    r = dev(x)
+    assert ref.ref_apply_rope_rmsnorm(ctypes.c_void_p(r.data_ptr()), seq_len, H, start_pos,
+                                      stream_ptr()) == 0
+    torch.cuda.synchronize()
+    dr = ulp_diff_bf16(bf16_to_u16(r), want)
+    assert dr.max() <= 1 and (dr == 0).mean() >= 0.99
+    # mine against the reference kernel directly
+    assert ulp_diff_bf16(got, bf16_to_u16(r)).max() <= 1
+
+
+@pytest.mark.parametrize("seq_len,start_pos", [(1, 0), (5, 100), (512, 1536)])
+def test_rope_qknorm_append(nc, seq_len, start_pos):
+    rows = start_pos + seq_len + 3
+    q = randn_u16((seq_len, H, D), 30)
+    k = randn_u16((seq_len, H, D), 31)
+    v = randn_u16((seq_len, H, D), 32)
+    kc0 = randn_u16((rows, H, D), 33)
+    vc0 = randn_u16((rows, H, D), 34)
+    wq, wkc, wvc = oracle.rope_qknorm_append(q, k, v, kc0, vc0, seq_len, H, start_pos)
+    tq, tk, tv, tkc, tvc = dev(q), dev(k), dev(v), dev(kc0), dev(vc0)
+    nc.rope_qknorm_append(tq, tk, tv, tkc, tvc, seq_len, H, start_pos)
+    assert ulp_diff_bf16(bf16_to_u16(tq), wq).max() <= 1
+    assert ulp_diff_bf16(bf16_to_u16(tkc), wkc).max() <= 1
+    assert np.array_equal(bf16_to_u16(tvc), wvc)
+    # inputs k, v untouched; rows outside the append window untouched
+    assert np.array_equal(bf16_to_u16(tk), k) and np.array_equal(bf16_to_u16(tv), v)
+    assert np.array_equal(bf16_to_u16(tkc)[:start_pos], kc0[:start_pos])
+    assert np.array_equal(bf16_to_u16(tkc)[start_pos + seq_len:], kc0[start_pos + seq_len:])
+
+
+# ----------------------------------------------------------------------------- prefill
+PREFILL_CASES = [
+    # (seq_q, kv_len, kv_offset)
+    (2, 2, 0),
+    (7, 7, 0),
+    (63, 63, 0),
+    (128, 128, 0),
+    (129, 129, 0),
+    (200, 1736, 1536),
+    (128, 2048, 1920),
+    (512, 2048, 1536),
+    (1, 1, 0),
+    (16, 100, 200),      # kv_offset beyond kv_len: every row sees all 100 keys
+    (300, 300, 0),
+]
+
+
+def _attention_case(nc, ref, seq_q, kv_len, off, seed, qk_scale=1.0, normalise=True,
+                    scale=SCALE):
+    q = randn_u16((seq_q, H, D), seed, qk_scale)
+    k = randn_u16((kv_len, H, D), seed + 1, qk_scale)
+    v = randn_u16((kv_len, H, D), seed + 2)
+    if normalise:
+        q = normed(q, max(off, 0))
+        k = normed(k, 0)
+    want = oracle.flash_attention(q, k, v, seq_q, kv_len, H, scale, off)
+    buf, out = guarded(seq_q * H * D)
+    nc.flash_attention(out, dev(q), dev(k), dev(v), seq_q, kv_len, H, scale, off)
+    torch.cuda.synchronize()
+    assert guards_intact(buf), "kernel wrote outside its output"
+    got = bf16_to_u16(out).reshape(seq_q, H * D)
+    assert_close_bf16(got, want, what=f"mine seq_q={seq_q} kv={kv_len} off={off}")
+    if ref is not None and seq_q * kv_len <= 600_000:
+        r = torch.empty((seq_q, H * D), dtype=torch.bfloat16, device="cuda")
+        tq, tk, tv = dev(q), dev(k), dev(v)
+        assert ref.ref_flash_attention(ctypes.c_void_p(r.data_ptr()), ctypes.c_void_p(tq.data_ptr()),
+                                       ctypes.c_void_p(tk.data_ptr()), ctypes.c_void_p(tv.data_ptr()),
+                                       seq_q, kv_len, H, float(scale), off, stream_ptr()) == 0
+        torch.cuda.synchronize()
+        rr = bf16_to_u16(r)
+        assert_close_bf16(rr, want, what="reference kernel vs oracle")
+        assert_close_bf16(got, rr, what="mine vs reference kernel")
+    return got, want
+
+
+@pytest.mark.parametrize("seq_q,kv_len,off", PREFILL_CASES)
+def test_flash_attention_prefill(nc, ref, seq_q, kv_len, off):
+    _attention_case(nc, ref, seq_q, kv_len, off, seed=1000 + seq_q + kv_len)
+
+
+def test_flash_attention_prefill_full_2048(nc, ref):
+    """cfg2 shape (2048 positions, causal, empty cache): against the oracle."""
+    _attention_case(nc, None, 2048, 2048, 0, seed=7)
+
+
+def test_flash_attention_prefill_wide_scores(nc):
+    """Unnormalised, scaled inputs (scores spread over tens of units) exercise the lazy
+    rescale of O and of the row sum."""
+    _attention_case(nc, None, 256, 640, 384, seed=99, qk_scale=3.0, normalise=False)
+
+
+def test_flash_attention_prefill_no_visible_key(nc):
+    """kv_offset < 0: leading rows see no key and become NaN, like the reference's 0/0."""
+    _attention_case(nc, None, 150, 150, -20, seed=5)
+
+
+def test_flash_attention_zero_kv(nc):
+    out = torch.zeros((3, H * D), dtype=torch.bfloat16, device="cuda")
+    z = torch.zeros((1, H, D), dtype=torch.bfloat16, device="cuda")
+    nc.flash_attention(out, torch.zeros((3, H, D), dtype=torch.bfloat16, device="cuda"), z, z,
+                       3, 0, H, SCALE, 0)
+    torch.cuda.synchronize()
+    assert torch.isnan(out.float()).all()
+
+
+# ----------------------------------------------------------------------------- decode
+@pytest.mark.parametrize("kv_len", [1, 2, 15, 16, 17, 63, 64, 129, 511, 512, 1536 + 512, 4097])
+def test_flash_attention_decode(nc, ref, kv_len):
+    """seq_q == 1 through the reference entry point (split-KV decode kernel)."""
+    _attention_case(nc, ref, 1, kv_len, kv_len - 1, seed=2000 + kv_len)
+
+
+def test_flash_attention_decode_offset_limits_keys(nc):
+    """Single query with kv_offset < kv_len - 1: only keys <= kv_offset are visible."""
+    _attention_case(nc, None, 1, 700, 300, seed=77)
+
+
+def _decode_batch(nc, lens, split_len, seed, fused=True, rows_extra=5):
+    B = len(lens)
+    max_len = max(lens)
+    rows = max_len + rows_extra
+    q = randn_u16((B, H, D), seed)
+    kn = randn_u16((B, H, D), seed + 1)
+    vn = randn_u16((B, H, D), seed + 2)
+    kcs, vcs = [], []
+    for b, L in enumerate(lens):
+        kc = normed(randn_u16((rows, H, D), seed + 10 + 2 * b), 0)
+        vc = randn_u16((rows, H, D), seed + 11 + 2 * b)
+        kcs.append(kc)
+        vcs.append(vc)
+    if fused:
+        want, wkc, wvc = oracle.decode_step(q, kn, vn, kcs, vcs, lens, H, SCALE)
+    else:
+        qn = np.stack([normed(q[b:b + 1], lens[b] - 1)[0] for b in range(B)])
+        want, wkc, wvc = oracle.decode_step(qn, None, None, kcs, vcs, lens, H, SCALE)
+        q = qn
+    tk = [dev(k) for k in kcs]
+    tv = [dev(v) for v in vcs]
+    kp = torch.tensor([t.data_ptr() for t in tk], dtype=torch.int64, device="cuda")
+    vp = torch.tensor([t.data_ptr() for t in tv], dtype=torch.int64, device="cuda")
+    lt = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(nc.decode_workspace_bytes(B, max_len, H, split_len), dtype=torch.uint8,
+                     device="cuda")
+    buf, out = guarded(B * H * D)
+    for _ in range(2):  # second call checks the self-resetting split counters
+        nc.decode_attention(out, dev(q), dev(kn) if fused else None, dev(vn) if fused else None,
+                            kp, vp, lt, H, SCALE, max_len, ws, split_len=split_len)
+        torch.cuda.synchronize()
+        got = bf16_to_u16(out).reshape(B, H * D)
+        assert_close_bf16(got, want, what=f"decode lens={lens} split={split_len}")
+    assert guards_intact(buf)
+    for b in range(B):
+        gk, gv = bf16_to_u16(tk[b]), bf16_to_u16(tv[b])
+        assert ulp_diff_bf16(gk, wkc[b]).max() <= 1, f"K cache of sequence {b}"
+        assert np.array_equal(gv, wvc[b]), f"V cache of sequence {b}"
+
+
+@pytest.mark.parametrize("split_len", [0, 16, 32, 128])
+def test_decode_batched_fused(nc, split_len):
+    _decode_batch(nc, [1, 2, 17, 100, 513, 1200], split_len, seed=300)
+
+
+def test_decode_batched_unfused(nc):
+    _decode_batch(nc, [3, 64, 65, 700], 0, seed=400, fused=False)
+
+
+def test_decode_cfg3_lengths_subset(nc):
+    """First 8 sequences of cfg3's kv_len draw (torch seed 2)."""
+    from nanochat_inferonly_lightning_b200 import workloads
+
+    _decode_batch(nc, workloads.cfg3_kv_lens()[:8], 0, seed=500)
+
+
+# ----------------------------------------------------------------------------- batched prefill
+@pytest.mark.parametrize("B,chunk,off,rows", [(2, 37, 100, 200), (3, 128, 1536, 2048),
+                                              (2, 512, 0, 600)])
+def test_prefill_batched(nc, B, chunk, off, rows):
+    q = np.stack([normed(randn_u16((chunk, H, D), 600 + b), off) for b in range(B)])
+    kslab = np.stack([normed(randn_u16((rows, H, D), 700 + b), 0) for b in range(B)])
+    vslab = np.stack([randn_u16((rows, H, D), 800 + b) for b in range(B)])
+    want = np.stack([oracle.flash_attention(q[b], kslab[b], vslab[b], chunk, off + chunk, H,
+                                            SCALE, off) for b in range(B)])
+    out = torch.empty((B, chunk, H * D), dtype=torch.bfloat16, device="cuda")
+    offs = torch.full((B,), off, dtype=torch.int32, device="cuda")
+    nc.prefill_attention_batched(out, dev(q), dev(kslab), dev(vslab), rows * H * D, rows, offs,
+                                 chunk, H, SCALE)
+    torch.cuda.synchronize()
+    assert_close_bf16(bf16_to_u16(out), want, what="batched prefill")
+
+
+# ----------------------------------------------------------------------------- KV cache object
+def test_kv_cache_prefill_then_decode(nc):
+    """Prefill a prompt through the cache object, then decode steps for two sequences; the
+    oracle replays the same sequence of appends."""
+    n_seqs, max_len, prompt = 2, 300, 40
+    cache = nc.KVCache(n_layers=2, n_seqs=n_seqs, max_len=max_len, heads=H)
+    layer = 1
+    okc = [np.zeros((max_len, H, D), np.uint16) for _ in range(n_seqs)]
+    ovc = [np.zeros((max_len, H, D), np.uint16) for _ in range(n_seqs)]
+    for s in range(n_seqs):
+        q = randn_u16((prompt, H, D), 900 + s)
+        k = randn_u16((prompt, H, D), 910 + s)
+        v = randn_u16((prompt, H, D), 920 + s)
+        wq, okc[s], ovc[s] = oracle.rope_qknorm_append(q, k, v, okc[s], ovc[s], prompt, H, 0)
+        want = oracle.flash_attention(wq, okc[s], ovc[s], prompt, prompt, H, SCALE, 0)
+        out = torch.empty((prompt, H * D), dtype=torch.bfloat16, device="cuda")
+        cache.prefill(layer, s, out, dev(q), dev(k), dev(v), prompt, SCALE)
+        torch.cuda.synchronize()
+        assert_close_bf16(bf16_to_u16(out), want, what="cache prefill")
+        assert cache.length(layer, s) == prompt
+    for step in range(3):
+        q = randn_u16((n_seqs, H, D), 950 + step)
+        kn = randn_u16((n_seqs, H, D), 960 + step)
+        vn = randn_u16((n_seqs, H, D), 970 + step)
+        lens = [cache.length(layer, s) + 1 for s in range(n_seqs)]
+        want, okc, ovc = oracle.decode_step(q, kn, vn, okc, ovc, lens, H, SCALE)
+        out = torch.empty((n_seqs, H * D), dtype=torch.bfloat16, device="cuda")
+        cache.decode(layer, out, dev(q), dev(kn), dev(vn), SCALE)
+        torch.cuda.synchronize()
+        assert_close_bf16(bf16_to_u16(out), want, what=f"cache decode step {step}")
+    for s in range(n_seqs):
+        assert cache.length(layer, s) == prompt + 3
+        assert ulp_diff_bf16(bf16_to_u16(cache.view(layer, s, "k")), okc[s]).max() <= 1
+        assert np.array_equal(bf16_to_u16(cache.view(layer, s, "v")), ovc[s])
+    cache.clear()
+    assert cache.length(layer, 0) == 0
+    cache.close()
+
+
+def test_device_status_clean(nc):
+    torch.cuda.synchronize()
+    assert nc.device_status() == 0
