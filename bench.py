@@ -45,40 +45,45 @@ FLUSH_BYTES = 256 << 20
 
 # ------------------------------------------------------------------------------ plumbing
 class Dist:
-    def __init__(self, n_gpus):
+    """One process per GPU (RANK / LOCAL_RANK / WORLD_SIZE from the launcher).  Collectives
+    are used only outside the timed regions: barriers around them and the max / sum of the
+    per-rank results.  backend="gloo" runs the same logic on CPU (tests)."""
+
+    def __init__(self, n_gpus, backend="nccl", timeout_s=120):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         if self.world != n_gpus:
             raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
-        torch.cuda.set_device(self.local)
+        self.device = "cuda" if backend == "nccl" else "cpu"
+        if backend == "nccl":
+            torch.cuda.set_device(self.local)
         self.pg = None
         if self.world > 1:
             import datetime
 
             import torch.distributed as dist
 
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {"device_id": torch.device("cuda", self.local)} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
             self.pg = dist
 
     def barrier(self):
         if self.pg:
             self.pg.barrier()
 
-    def max(self, x):
+    def _reduce(self, x, op):
         if not self.pg:
             return x
-        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, x):
+        return self._reduce(x, self.pg.ReduceOp.MAX if self.pg else None)
+
     def sum(self, x):
-        if not self.pg:
-            return x
-        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
+        return self._reduce(x, self.pg.ReduceOp.SUM if self.pg else None)
 
     def close(self):
         if self.pg:
@@ -509,6 +514,8 @@ def main():
     ap.add_argument("--impl", choices=["nc", "reference"], default="nc")
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4"], default=None,
+                    help="run one workload only (profiling); implies --no-cpu, no e2e")
     args = ap.parse_args()
     K, Wm = args.steps, max(args.warmup, 3)
 
@@ -526,6 +533,18 @@ def main():
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     stepper = Stepper(dist, flush)
 
+    if args.only:
+        fn = {"prefill": lambda: bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic, False),
+              "cfg1": lambda: bench_decode(impl, dist, stepper, K, Wm, peaks, traffic,
+                                           [W.CFG1_LEN], "cfg1"),
+              "cfg3": lambda: bench_decode(impl, dist, stepper, K, Wm, peaks, traffic,
+                                           W.cfg3_kv_lens(), "cfg3"),
+              "cfg4": lambda: bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic)}[args.only]
+        r = fn()
+        if dist.rank == 0:
+            print(json.dumps({"only": args.only, "impl": args.impl, **r}), flush=True)
+        dist.close()
+        return
     clocks = ClockSampler(dist.local)
     clocks.start()
     head = bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic)

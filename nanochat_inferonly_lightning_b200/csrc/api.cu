@@ -95,15 +95,17 @@ struct WsLayout {
     unsigned* counters;
 };
 
+// Workspace layout: the split counters come first, at a fixed offset, so calls with a
+// different number of splits find them where the previous call left them (at zero).
 WsLayout carve_ws(void* ws, int batch, int max_splits, int heads) {
     const size_t n = (size_t)batch * max_splits * heads;
     uint8_t* p = static_cast<uint8_t*>(ws);
     WsLayout w;
-    w.part_o = reinterpret_cast<float*>(p);
-    size_t off = (n * kHeadDim * sizeof(float) + 255) & ~(size_t)255;
+    w.counters = reinterpret_cast<unsigned*>(p);
+    size_t off = ((size_t)batch * sizeof(unsigned) + 255) & ~(size_t)255;
     w.part_ml = reinterpret_cast<float2*>(p + off);
     off = (off + n * sizeof(float2) + 255) & ~(size_t)255;
-    w.counters = reinterpret_cast<unsigned*>(p + off);
+    w.part_o = reinterpret_cast<float*>(p + off);
     return w;
 }
 

@@ -218,29 +218,47 @@ __global__ void __launch_bounds__(1024) decode_kernel(DecodeArgs a) {
     __syncthreads();
     if (s_ticket != (unsigned)(n_splits - 1)) return;
 
-    // Last CTA of this sequence: combine every split.  Lane owns dims [4*lane, 4*lane+4).
+    // Last CTA of this sequence: combine every split.  Warp h = head h; lanes read the
+    // split maxima in parallel, then each lane owns dims [4*lane, 4*lane+4) and keeps eight
+    // splits' partial rows in flight per round.
     __threadfence();
     if (threadIdx.x == 0) a.counters[b] = 0u;  // ready for the next launch
-    const size_t base = (size_t)b * a.max_splits * H + h;
+    const size_t base = (size_t)b * a.max_splits * H + h;  // (b, split 0, h); split stride H
     float M = kNegInf;
-    for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(a.part_ml + base + (size_t)sp * H).x);
+    for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(a.part_ml + base + (size_t)sp * H).x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
     const float mu = (M == kNegInf) ? 0.f : M;
-    float den = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int sp = 0; sp < n_splits; ++sp) {
-        const size_t pi = base + (size_t)sp * H;
-        const float2 ml = __ldcg(a.part_ml + pi);
-        const float w = fast_exp2(ml.x - mu);
-        den = __fmaf_rn(ml.y, w, den);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * kHeadDim) + lane);
-        o[0] = __fmaf_rn(v.x, w, o[0]);
-        o[1] = __fmaf_rn(v.y, w, o[1]);
-        o[2] = __fmaf_rn(v.z, w, o[2]);
-        o[3] = __fmaf_rn(v.w, w, o[3]);
+    float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
+        float2 ml[8];
+        float4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int sp = sp0 + i;
+            if (sp < n_splits) {
+                const size_t pi = base + (size_t)sp * H;
+                ml[i] = __ldcg(a.part_ml + pi);
+                v[i] = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * kHeadDim) + lane);
+            } else {
+                ml[i] = make_float2(kNegInf, 0.f);
+                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float w = fast_exp2(ml[i].x - mu);
+            den = __fmaf_rn(ml[i].y, w, den);
+            o4[0] = __fmaf_rn(v[i].x, w, o4[0]);
+            o4[1] = __fmaf_rn(v[i].y, w, o4[1]);
+            o4[2] = __fmaf_rn(v[i].z, w, o4[2]);
+            o4[3] = __fmaf_rn(v[i].w, w, o4[3]);
+        }
     }
     const float inv = 1.0f / den;
     uint2 r;
-    r.x = pack_bf16x2(o[0] * inv, o[1] * inv);
-    r.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+    r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
+    r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
     *reinterpret_cast<uint2*>(out_row + (size_t)h * kHeadDim + 4 * lane) = r;
 }
 
@@ -248,11 +266,9 @@ __global__ void __launch_bounds__(1024) decode_kernel(DecodeArgs a) {
 
 size_t decode_workspace_bytes(int batch, int max_splits, int heads) {
     const size_t n = (size_t)batch * max_splits * heads;
-    size_t bytes = n * kHeadDim * sizeof(float);           // part_o
-    bytes = (bytes + 255) & ~(size_t)255;
-    bytes += n * sizeof(float2);                           // part_ml
-    bytes = (bytes + 255) & ~(size_t)255;
-    bytes += (size_t)batch * sizeof(unsigned);             // counters
+    size_t bytes = ((size_t)batch * sizeof(unsigned) + 255) & ~(size_t)255;  // counters
+    bytes = (bytes + n * sizeof(float2) + 255) & ~(size_t)255;                 // part_ml
+    bytes += n * kHeadDim * sizeof(float);                                     // part_o
     return (bytes + 255) & ~(size_t)255;
 }
 

@@ -71,6 +71,7 @@ struct PrefillKParams {
     int seq_q;
     int heads;
     int n_qtiles;
+    int num_sms;
     float scale_log2;
     int* status;
 };
@@ -97,11 +98,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint64_t* bars = tail->bars;
     volatile int* abort_flag = &tail->abort;
 
-    // Longest-first tile order: consecutive block indices walk all (head, seq) groups of
-    // the last (longest) query tile first.
+    // Work order.  Items are ranked longest first (the last query tile of every (head, seq)
+    // group first).  Blocks [0, num_sms) take items [0, num_sms); later blocks take the
+    // remaining items shortest first, so an SM that receives block i and block num_sms + i
+    // holds one long and one short tile and the per-SM sums come out nearly equal.
     const int groups = p.heads * p.batch;
-    const int rank = blockIdx.x / groups;
-    const int g = blockIdx.x - rank * groups;
+    const int total = p.n_qtiles * groups;
+    const int bid = blockIdx.x;
+    const int item = (bid < p.num_sms) ? bid : total - 1 - (bid - p.num_sms);
+    const int rank = item / groups;
+    const int g = item - rank * groups;
     const int t = p.n_qtiles - 1 - rank;
     const int h = g % p.heads;
     const int b = g / p.heads;
@@ -388,6 +394,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     kp.seq_q = a.seq_q;
     kp.heads = a.heads;
     kp.n_qtiles = (a.seq_q + kBM - 1) / kBM;
+    static int sm_count[64] = {};
+    if (!sm_count[dev]) {
+        cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    kp.num_sms = sm_count[dev];
     kp.scale_log2 = a.scale * kLog2e;
     kp.status = a.status;
     const long long nblocks = (long long)kp.n_qtiles * a.heads * a.batch;

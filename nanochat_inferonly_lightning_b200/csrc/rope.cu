@@ -21,36 +21,58 @@ namespace {
 // cos/sin table (10.5 MB per device), filled by upload_rope_table().
 __device__ float2 g_rope_cs[kRopeMaxSeq * kHalfDim];
 
-constexpr int kRopeThreads = 256;  // 16 rows per block
+constexpr int kRopeThreads = 256;   // 16 half-warps per block
+constexpr int kRowsPerHalfWarp = 2;  // rows per half-warp: all loads issued before any math
 
 template <int MODE>
 __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
-    const int gtid = blockIdx.x * kRopeThreads + threadIdx.x;
-    const int row = gtid >> 4;  // (position, head) row handled by this half-warp
+    const int hw = (blockIdx.x * kRopeThreads + threadIdx.x) >> 4;
     const int sub = threadIdx.x & 15;
     const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
     const int nrows = a.seq_len * a.heads;
-    if (row >= nrows) return;  // whole half-warps leave together
-    const int s = row / a.heads;
-    const int pos = a.start_pos + s;
-    const size_t off = (size_t)row * kHeadDim + 8 * sub;
-
+    const int row0 = hw * kRowsPerHalfWarp;
+    if (row0 >= nrows) return;  // whole half-warps leave together
+    bool has[kRowsPerHalfWarp];
+    size_t off[kRowsPerHalfWarp];
+    int pos[kRowsPerHalfWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+        const int row = row0 + r;
+        has[r] = row < nrows;
+        off[r] = (size_t)(has[r] ? row : row0) * kHeadDim + 8 * sub;
+        pos[r] = a.start_pos + (has[r] ? row : row0) / a.heads;
+    }
     if (MODE == kRopeNormAppend) {
-        // Issue all three loads before any math.
-        const uint4 qr = *reinterpret_cast<const uint4*>(a.q + off);
-        const uint4 kr = *reinterpret_cast<const uint4*>(a.k + off);
-        const uint4 vr = *reinterpret_cast<const uint4*>(a.v + off);
-        float y[8];
-        rope_norm_row(a.rope_cs, qr, sub, mask, pos, true, y);
-        *reinterpret_cast<uint4*>(a.q + off) = f32_to_bf16x8(y);
-        rope_norm_row(a.rope_cs, kr, sub, mask, pos, true, y);
-        *reinterpret_cast<uint4*>(a.k_dst + off) = f32_to_bf16x8(y);
-        *reinterpret_cast<uint4*>(a.v_dst + off) = vr;
+        uint4 qr[kRowsPerHalfWarp], kr[kRowsPerHalfWarp], vr[kRowsPerHalfWarp];
+#pragma unroll
+        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+            qr[r] = *reinterpret_cast<const uint4*>(a.q + off[r]);
+            kr[r] = *reinterpret_cast<const uint4*>(a.k + off[r]);
+            vr[r] = *reinterpret_cast<const uint4*>(a.v + off[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+            float y[8];
+            rope_norm_row(a.rope_cs, qr[r], sub, mask, pos[r], true, y);
+            const uint4 qo = f32_to_bf16x8(y);
+            rope_norm_row(a.rope_cs, kr[r], sub, mask, pos[r], true, y);
+            const uint4 ko = f32_to_bf16x8(y);
+            if (has[r]) {
+                *reinterpret_cast<uint4*>(a.q + off[r]) = qo;
+                *reinterpret_cast<uint4*>(a.k_dst + off[r]) = ko;
+                *reinterpret_cast<uint4*>(a.v_dst + off[r]) = vr[r];
+            }
+        }
     } else {
-        const uint4 xr = *reinterpret_cast<const uint4*>(a.q + off);
-        float y[8];
-        rope_norm_row(a.rope_cs, xr, sub, mask, pos, MODE == kRopeNorm, y);
-        *reinterpret_cast<uint4*>(a.q + off) = f32_to_bf16x8(y);
+        uint4 xr[kRowsPerHalfWarp];
+#pragma unroll
+        for (int r = 0; r < kRowsPerHalfWarp; ++r) xr[r] = *reinterpret_cast<const uint4*>(a.q + off[r]);
+#pragma unroll
+        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
+            float y[8];
+            rope_norm_row(a.rope_cs, xr[r], sub, mask, pos[r], MODE == kRopeNorm, y);
+            if (has[r]) *reinterpret_cast<uint4*>(a.q + off[r]) = f32_to_bf16x8(y);
+        }
     }
 }
 
@@ -59,7 +81,8 @@ __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
 cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream) {
     const long long rows = (long long)a.seq_len * a.heads;
     if (rows <= 0) return cudaSuccess;
-    const long long threads = rows * 16;
+    const long long halfwarps = (rows + kRowsPerHalfWarp - 1) / kRowsPerHalfWarp;
+    const long long threads = halfwarps * 16;
     const unsigned blocks = (unsigned)((threads + kRopeThreads - 1) / kRopeThreads);
     switch (mode) {
         case kRopeOnly:
