@@ -58,6 +58,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, for x <= 8 (anything below -127 gives 0): range reduction
+// x = n + f with n = round(x) and f in [-1/2, 1/2] (the 1.5 * 2^23 rounding trick), a cubic
+// for 2^f, and n added straight into the exponent bits.  The cubic 1 + c1 f + c2 f^2 + c3 f^3
+// is a minimax fit of 2^f on [-1/2, 1/2] with the constant term pinned to 1 (made for this
+// kernel; max relative error 1.0e-4, against 3.9e-3 for one bf16 half-ulp), so x = -127
+// yields exactly +0.  Used for part of the softmax exponentials to relieve the MUFU pipe.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -127.0f);
+    const float r = x + 12582912.0f;
+    const float f = x - (r - 12582912.0f);
+    float p = __fmaf_rn(0.05500893f, f, 0.24221095f);
+    p = __fmaf_rn(p, f, 0.6932829f);
+    p = __fmaf_rn(p, f, 1.0f);
+    return __int_as_float(__float_as_int(p) + ((__float_as_int(r) - 0x4B400000) << 23));
+}
+
 // RoPE (+ optional parameter-free RMSNorm) of one 128-wide head row held by a half-warp:
 // lane `sub` (0..15) owns dims [8*sub, 8*sub+8).  Half-split pairing (dim i with i+64,
 // reference kernels/rope.cu:95-97) puts a lane's partner at sub^8.  `mask` is the

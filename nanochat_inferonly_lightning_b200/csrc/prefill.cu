@@ -8,15 +8,16 @@
 // blocks of 128; only blocks that hold a visible key are visited (causal rule
 // key <= query + kv_offset and key < kv_len, reference flash_attention.cu:37, :74).
 //
-// Roles (192 threads):
-//   warp 0      TMA producer: Q tile once, then K(j), V(j) into single-buffered tiles.
-//   warp 1      allocates 256 TMEM columns; one lane issues every tcgen05.mma.
+// Roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: the Q tile once, then K(j) and V(j) into two-stage rings.
+//   warp 1      allocates all 512 TMEM columns; one lane issues every tcgen05.mma.
 //   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
-// Tensor memory: S = Q.K^T (fp32, columns [0,128)); P (bf16 pairs) overwrites S columns
-// [0,64) and feeds the P.V MMA straight from TMEM; O (fp32) in columns [128,256).
-// Per key block j:   QK(j) -> softmax(j) -> PV(j) -> QK(j+1) ...
-// Two CTAs share each SM (96 KB smem, 256 TMEM columns each), so one CTA's softmax runs
-// while the other's MMAs occupy the tensor pipe.
+// Tensor memory (512 columns): S0 [0,128) and S1 [128,256) hold Q.K^T of consecutive key
+// blocks (fp32); O [256,384) accumulates P.V (fp32); P0 [384,448) and P1 [448,512) hold the
+// bf16 probabilities (two per column) that feed the P.V MMA straight from TMEM.
+// Pipeline: the MMA warp keeps QK two blocks ahead of the softmax, so while the softmax of
+// block j+1 runs, the tensor pipe executes PV(j) and QK(j+2); the softmax warps go from one
+// block to the next without waiting for the tensor pipe.
 //
 // Softmax: fp32, base-2 exponentials of scale*log2(e)-scaled scores, with a lazily updated
 // reference max: O and the row sum are rescaled only when a block's max exceeds the
@@ -36,20 +37,23 @@ constexpr int kBN = 128;             // keys per block
 constexpr int kThreads = 192;
 constexpr uint32_t kBoxBytes = 64 * 128 * 2;    // one 64-dim x 128-row box, 128B swizzle
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 x 128 bf16
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;        // S0 at 0, S1 at 128
+constexpr uint32_t kColO = 256;
+constexpr uint32_t kColP = 384;      // P0 at 384, P1 at 448
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kNegInf = -__builtin_huge_valf();
 
 enum Bar : int {
     kBarQ = 0,
-    kBarKFull,
-    kBarKFree,
-    kBarVFull,
-    kBarVFree,
-    kBarS,
-    kBarP,
-    kBarO,
-    kBarOFinal,
+    kBarKFull,   // [2]
+    kBarKFree = kBarKFull + 2,
+    kBarVFull = kBarKFree + 2,
+    kBarVFree = kBarVFull + 2,
+    kBarS = kBarVFree + 2,
+    kBarP = kBarS + 2,
+    kBarPV = kBarP + 2,
+    kBarOFinal = kBarPV + 2,
     kNumBars
 };
 
@@ -59,7 +63,8 @@ struct __align__(8) SmemTail {
     int abort;
 };
 
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 3 * kTileBytes + sizeof(SmemTail);
+// Q tile + two K stages + two V stages.
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 5 * kTileBytes + sizeof(SmemTail);
 
 struct PrefillKParams {
     bf16* out;
@@ -85,29 +90,23 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* t
         : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const PrefillKParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sQ = smem;
-    uint8_t* sK = smem + kTileBytes;
-    uint8_t* sV = smem + 2 * kTileBytes;
-    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 3 * kTileBytes);
+    uint8_t* sK = smem + kTileBytes;       // stages at sK, sK + kTileBytes
+    uint8_t* sV = smem + 3 * kTileBytes;   // stages at sV, sV + kTileBytes
+    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 5 * kTileBytes);
     uint64_t* bars = tail->bars;
     volatile int* abort_flag = &tail->abort;
 
-    // Work order.  Items are ranked longest first (the last query tile of every (head, seq)
-    // group first).  Blocks [0, num_sms) take items [0, num_sms); later blocks take the
-    // remaining items shortest first, so an SM that receives block i and block num_sms + i
-    // holds one long and one short tile and the per-SM sums come out nearly equal.
+    // Work order: longest query tiles first (the last tile of every (head, seq) group).
     const int groups = p.heads * p.batch;
-    const int total = p.n_qtiles * groups;
-    const int bid = blockIdx.x;
-    const int item = (bid < p.num_sms) ? bid : total - 1 - (bid - p.num_sms);
-    const int rank = item / groups;
-    const int g = item - rank * groups;
+    const int rank = blockIdx.x / groups;
+    const int g = blockIdx.x - rank * groups;
     const int t = p.n_qtiles - 1 - rank;
     const int h = g % p.heads;
     const int b = g / p.heads;
@@ -122,7 +121,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], i == kBarP ? 128u : 1u);
+        for (int i = 0; i < kNumBars; ++i)
+            mbar_init(&bars[i], (i == kBarP || i == kBarP + 1) ? 128u : 1u);
         tail->abort = 0;
         fence_mbar_init();
     }
@@ -139,8 +139,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
-    const uint32_t tS = tmem;        // S (fp32) / P (bf16x2, first 64 columns)
-    const uint32_t tO = tmem + 128;  // O (fp32)
 
     if (warp == 0) {
         // ------------------------------------------------------------------ producer
@@ -149,18 +147,25 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
             tma_load_3d(sQ, &tmQ, &bars[kBarQ], x0, q0, b);
             tma_load_3d(sQ + kBoxBytes, &tmQ, &bars[kBarQ], x0 + 64, q0, b);
-            for (int j = 0; j < nb; ++j) {
-                if (j > 0 && !mbar_wait(&bars[kBarKFree], (j - 1) & 1, abort_flag, p.status, 1)) break;
-                mbar_arrive_expect_tx(&bars[kBarKFull], kTileBytes);
-                tma_load_3d(sK, &tmK, &bars[kBarKFull], x0, j * kBN, b);
-                tma_load_3d(sK + kBoxBytes, &tmK, &bars[kBarKFull], x0 + 64, j * kBN, b);
-                if (j > 0 && !mbar_wait(&bars[kBarVFree], (j - 1) & 1, abort_flag, p.status, 2)) break;
-                mbar_arrive_expect_tx(&bars[kBarVFull], kTileBytes);
-                tma_load_3d(sV, &tmV, &bars[kBarVFull], x0, j * kBN, b);
-                tma_load_3d(sV + kBoxBytes, &tmV, &bars[kBarVFull], x0 + 64, j * kBN, b);
+            bool ok = true;
+            for (int j = 0; ok && j < nb; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = ((j >> 1) - 1) & 1;  // phase of the previous use of stage st
+                if (j >= 2 && !mbar_wait(&bars[kBarKFree + st], ph, abort_flag, p.status, 1)) break;
+                uint8_t* dk = sK + st * kTileBytes;
+                mbar_arrive_expect_tx(&bars[kBarKFull + st], kTileBytes);
+                tma_load_3d(dk, &tmK, &bars[kBarKFull + st], x0, j * kBN, b);
+                tma_load_3d(dk + kBoxBytes, &tmK, &bars[kBarKFull + st], x0 + 64, j * kBN, b);
+                if (j >= 2 && !mbar_wait(&bars[kBarVFree + st], ph, abort_flag, p.status, 2)) break;
+                uint8_t* dv = sV + st * kTileBytes;
+                mbar_arrive_expect_tx(&bars[kBarVFull + st], kTileBytes);
+                tma_load_3d(dv, &tmV, &bars[kBarVFull + st], x0, j * kBN, b);
+                tma_load_3d(dv + kBoxBytes, &tmV, &bars[kBarVFull + st], x0 + 64, j * kBN, b);
             }
-            // Do not leave the CTA with loads still landing in shared memory.
-            mbar_wait(&bars[kBarVFree], (nb - 1) & 1, abort_flag, p.status, 3);
+            // Do not leave the CTA with loads still landing in shared memory: the last V
+            // load of each stage is consumed by a PV whose completion arrives on kBarVFree.
+            for (int j = max(nb - 2, 0); j < nb; ++j)
+                mbar_wait(&bars[kBarVFree + (j & 1)], (j >> 1) & 1, abort_flag, p.status, 3);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -169,36 +174,46 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
             const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
             const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-            bool ok = mbar_wait(&bars[kBarQ], 0, abort_flag, p.status, 4);
-            for (int j = 0; ok && j < nb; ++j) {
-                if (!mbar_wait(&bars[kBarKFull], j & 1, abort_flag, p.status, 5)) break;
+            auto issue_qk = [&](int j) -> bool {
+                const int st = j & 1;
+                if (!mbar_wait(&bars[kBarKFull + st], (j >> 1) & 1, abort_flag, p.status, 5))
+                    return false;
                 tc_fence_after();
+                const uint32_t ak = aK + st * kTileBytes;
+                const uint32_t ts = tmem + kColS + st * 128;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t koff = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(tS, smem_desc_sw128(aQ + koff, 16, 1024),
-                           smem_desc_sw128(aK + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+                    mma_ss(ts, smem_desc_sw128(aQ + koff, 16, 1024),
+                           smem_desc_sw128(ak + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&bars[kBarKFree]);
-                mma_commit(&bars[kBarS]);
-                if (!mbar_wait(&bars[kBarP], j & 1, abort_flag, p.status, 6)) break;
-                if (!mbar_wait(&bars[kBarVFull], j & 1, abort_flag, p.status, 7)) break;
+                mma_commit(&bars[kBarKFree + st]);
+                mma_commit(&bars[kBarS + st]);
+                return true;
+            };
+            bool ok = mbar_wait(&bars[kBarQ], 0, abort_flag, p.status, 4);
+            ok = ok && issue_qk(0);
+            if (ok && nb > 1) ok = issue_qk(1);
+            for (int j = 0; ok && j < nb; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6)) break;
+                if (!mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7)) break;
                 tc_fence_after();
+                const uint32_t av = aV + st * kTileBytes;
+                const uint32_t tp = tmem + kColP + st * 64;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     // 16 keys per MMA: P columns [8kk, 8kk+8) (bf16 pairs), V rows
                     // [16kk, 16kk+16) = two 8-row swizzle groups.
-                    mma_ts(tO, tS + kk * 8, smem_desc_sw128(aV + kk * 2048, kBoxBytes, 1024),
+                    mma_ts(tmem + kColO, tp + kk * 8, smem_desc_sw128(av + kk * 2048, kBoxBytes, 1024),
                            idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&bars[kBarVFree]);
-                if (j + 1 < nb) {
-                    // P aliases S: the next QK must not start before this PV has read P.
-                    mma_commit(&bars[kBarO]);
-                    if (!mbar_wait(&bars[kBarO], j & 1, abort_flag, p.status, 8)) break;
-                } else {
-                    mma_commit(&bars[kBarOFinal]);
-                }
+                mma_commit(&bars[kBarVFree + st]);
+                mma_commit(&bars[kBarPV + st]);
+                if (j + 1 == nb) mma_commit(&bars[kBarOFinal]);
+                // softmax(j) has read S(j & 1) (it wrote P(j) afterwards): refill it.
+                if (j + 2 < nb) ok = issue_qk(j + 2);
             }
         }
         __syncwarp();
@@ -209,26 +224,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int q = q0 + r;
         const int qlim = q + off;  // last visible key for this row
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t tO = tmem + kColO + lane_base;
         const float sl2 = p.scale_log2;
         float m_ref = kNegInf, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nb; ++j) {
-            // Warp-uniform outcome: the TMEM loads below are warp-collective.
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarS], j & 1, abort_flag, p.status, 9))) {
+            const int st = j & 1;
+            // Warp-uniform outcome: the TMEM accesses below are warp-collective.
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarS + st], (j >> 1) & 1, abort_flag,
+                                                   p.status, 9))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
+            uint32_t sraw[128];
+            tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
             float s[128];
-            {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t raw[32];
-                    tmem_ld32_sync(tS + lane_base + 32 * c, raw);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(raw[i]);
-                }
-            }
+            for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
             const int key0 = j * kBN;
             if (key0 + kBN - 1 > q0 + off || key0 + kBN > kv_len) {
 #pragma unroll
@@ -237,9 +250,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                     if (key > qlim || key >= kv_len) s[c] = kNegInf;
                 }
             }
-            float bm = s[0];
+            // Row max: eight independent partial maxima (short dependency chains).
+            float pm[8];
 #pragma unroll
-            for (int c = 1; c < 128; ++c) bm = fmaxf(bm, s[c]);
+            for (int i = 0; i < 8; ++i) pm[i] = s[i];
+#pragma unroll
+            for (int c = 8; c < 128; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+            const float bm = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
             const float bm2 = bm * sl2;
             const bool renew = (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
             float alpha = 1.f;
@@ -248,35 +266,51 @@ __global__ void __launch_bounds__(kThreads, 2)
                 m_ref = bm2;
             }
             l *= alpha;
-            // O holds the sum through PV(j-1) and is idle now; rescale rows that renewed.
+            // Rescale O for rows that renewed; O must first hold PV(j-1) complete.
             if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
+                const int sp = (j - 1) & 1;
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + sp], ((j - 1) >> 1) & 1,
+                                                       abort_flag, p.status, 11))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t raw[32];
-                    tmem_ld32_sync(tO + lane_base + 32 * c, raw);
+                    tmem_ld32_sync(tO + 32 * c, raw);
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
-                    tmem_st32_sync(tO + lane_base + 32 * c, raw);
+                    tmem_st32_sync(tO + 32 * c, raw);
                 }
             }
             const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
-            float rowsum = 0.f;
+            // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.
+            float ps[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[64];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t pk[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float p0 = fast_exp2(__fmaf_rn(s[64 * c + 2 * i], sl2, -mu));
-                    const float p1 = fast_exp2(__fmaf_rn(s[64 * c + 2 * i + 1], sl2, -mu));
-                    rowsum += p0 + p1;
-                    pk[i] = pack_bf16x2(p0, p1);
-                }
-                tmem_st32_sync(tS + lane_base + 32 * c, pk);
+            for (int i = 0; i < 64; ++i) {
+                // One pair in four goes through the FMA-pipe polynomial, the rest through MUFU.
+                const float x0 = __fmaf_rn(s[2 * i], sl2, -mu);
+                const float x1 = __fmaf_rn(s[2 * i + 1], sl2, -mu);
+                const bool poly = (i & 3) == 3;
+                const float p0 = poly ? exp2_poly(x0) : fast_exp2(x0);
+                const float p1 = poly ? exp2_poly(x1) : fast_exp2(x1);
+                ps[i & 3] += p0 + p1;
+                pk[i] = pack_bf16x2(p0, p1);
             }
-            l += rowsum;
+            // P(j & 1) was last read by PV(j-2); wait for it before overwriting.
+            if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + st], ((j - 2) >> 1) & 1,
+                                                             abort_flag, p.status, 12))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
+            l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             tc_fence_before();
-            mbar_arrive(&bars[kBarP]);
+            mbar_arrive(&bars[kBarP + st]);
         }
         // Epilogue: O / l -> bf16 -> out[b, q, h, :].
         bf16* orow = p.out + (((size_t)b * p.seq_q + q) * p.heads + h) * kHeadDim;
@@ -294,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t raw[32];
-                tmem_ld32_sync(tO + lane_base + 32 * c, raw);
+                tmem_ld32_sync(tO + 32 * c, raw);
                 if (store) {
                     uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
@@ -399,7 +433,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
     }
-    kp.num_sms = sm_count[dev];
+    kp.num_sms = sm_count[dev];  // kept for schedulers that place work per SM
     kp.scale_log2 = a.scale * kLog2e;
     kp.status = a.status;
     const long long nblocks = (long long)kp.n_qtiles * a.heads * a.batch;

@@ -8,6 +8,7 @@
 // Mapping: one half-warp per (position, head) row, 16 lanes x 16-byte loads = one 256-byte
 // head row, so a warp moves two full rows per instruction (fully coalesced).  The pair
 // partner (dim i <-> i+64) sits eight lanes away and is fetched with one shuffle per word.
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 #include <vector>
@@ -21,58 +22,56 @@ namespace {
 // cos/sin table (10.5 MB per device), filled by upload_rope_table().
 __device__ float2 g_rope_cs[kRopeMaxSeq * kHalfDim];
 
-constexpr int kRopeThreads = 256;   // 16 half-warps per block
-constexpr int kRowsPerHalfWarp = 2;  // rows per half-warp: all loads issued before any math
+constexpr int kRopeThreads = 256;  // 16 half-warps per block
+constexpr int kRopeBlocksPerSm = 4;
 
+// One (position, head) row's inputs for one lane: 16 bytes of q (or x), k and v.
+struct RowIn {
+    uint4 q, k, v;
+};
+
+template <int MODE>
+__device__ __forceinline__ RowIn load_row(const RopeArgs& a, size_t off) {
+    RowIn r;
+    r.q = __ldcs(reinterpret_cast<const uint4*>(a.q + off));
+    if (MODE == kRopeNormAppend) {
+        r.k = __ldcs(reinterpret_cast<const uint4*>(a.k + off));
+        r.v = __ldcs(reinterpret_cast<const uint4*>(a.v + off));
+    }
+    return r;
+}
+
+// Persistent, grid-stride streaming pass: each half-warp walks rows row, row + stride, ...
+// and issues the loads of its next row before it computes the current one, so every lane
+// keeps two rows of loads in flight.
 template <int MODE>
 __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
     const int hw = (blockIdx.x * kRopeThreads + threadIdx.x) >> 4;
+    const int stride = (gridDim.x * kRopeThreads) >> 4;
     const int sub = threadIdx.x & 15;
     const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
     const int nrows = a.seq_len * a.heads;
-    const int row0 = hw * kRowsPerHalfWarp;
-    if (row0 >= nrows) return;  // whole half-warps leave together
-    bool has[kRowsPerHalfWarp];
-    size_t off[kRowsPerHalfWarp];
-    int pos[kRowsPerHalfWarp];
-#pragma unroll
-    for (int r = 0; r < kRowsPerHalfWarp; ++r) {
-        const int row = row0 + r;
-        has[r] = row < nrows;
-        off[r] = (size_t)(has[r] ? row : row0) * kHeadDim + 8 * sub;
-        pos[r] = a.start_pos + (has[r] ? row : row0) / a.heads;
-    }
-    if (MODE == kRopeNormAppend) {
-        uint4 qr[kRowsPerHalfWarp], kr[kRowsPerHalfWarp], vr[kRowsPerHalfWarp];
-#pragma unroll
-        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
-            qr[r] = *reinterpret_cast<const uint4*>(a.q + off[r]);
-            kr[r] = *reinterpret_cast<const uint4*>(a.k + off[r]);
-            vr[r] = *reinterpret_cast<const uint4*>(a.v + off[r]);
+    int row = hw;
+    if (row >= nrows) return;  // whole half-warps leave together
+    RowIn cur = load_row<MODE>(a, (size_t)row * kHeadDim + 8 * sub);
+    for (; row < nrows; row += stride) {
+        const int next = row + stride;
+        RowIn nxt;
+        if (next < nrows) nxt = load_row<MODE>(a, (size_t)next * kHeadDim + 8 * sub);
+        const size_t off = (size_t)row * kHeadDim + 8 * sub;
+        const int pos = a.start_pos + row / a.heads;
+        float y[8];
+        if (MODE == kRopeNormAppend) {
+            rope_norm_row(a.rope_cs, cur.q, sub, mask, pos, true, y);
+            __stcs(reinterpret_cast<uint4*>(a.q + off), f32_to_bf16x8(y));
+            rope_norm_row(a.rope_cs, cur.k, sub, mask, pos, true, y);
+            *reinterpret_cast<uint4*>(a.k_dst + off) = f32_to_bf16x8(y);
+            *reinterpret_cast<uint4*>(a.v_dst + off) = cur.v;
+        } else {
+            rope_norm_row(a.rope_cs, cur.q, sub, mask, pos, MODE == kRopeNorm, y);
+            *reinterpret_cast<uint4*>(a.q + off) = f32_to_bf16x8(y);
         }
-#pragma unroll
-        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
-            float y[8];
-            rope_norm_row(a.rope_cs, qr[r], sub, mask, pos[r], true, y);
-            const uint4 qo = f32_to_bf16x8(y);
-            rope_norm_row(a.rope_cs, kr[r], sub, mask, pos[r], true, y);
-            const uint4 ko = f32_to_bf16x8(y);
-            if (has[r]) {
-                *reinterpret_cast<uint4*>(a.q + off[r]) = qo;
-                *reinterpret_cast<uint4*>(a.k_dst + off[r]) = ko;
-                *reinterpret_cast<uint4*>(a.v_dst + off[r]) = vr[r];
-            }
-        }
-    } else {
-        uint4 xr[kRowsPerHalfWarp];
-#pragma unroll
-        for (int r = 0; r < kRowsPerHalfWarp; ++r) xr[r] = *reinterpret_cast<const uint4*>(a.q + off[r]);
-#pragma unroll
-        for (int r = 0; r < kRowsPerHalfWarp; ++r) {
-            float y[8];
-            rope_norm_row(a.rope_cs, xr[r], sub, mask, pos[r], MODE == kRopeNorm, y);
-            if (has[r]) *reinterpret_cast<uint4*>(a.q + off[r]) = f32_to_bf16x8(y);
-        }
+        cur = nxt;
     }
 }
 
@@ -81,9 +80,18 @@ __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
 cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream) {
     const long long rows = (long long)a.seq_len * a.heads;
     if (rows <= 0) return cudaSuccess;
-    const long long halfwarps = (rows + kRowsPerHalfWarp - 1) / kRowsPerHalfWarp;
-    const long long threads = halfwarps * 16;
-    const unsigned blocks = (unsigned)((threads + kRopeThreads - 1) / kRopeThreads);
+    static int sms[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!sms[dev]) {
+        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    // Enough half-warps for every row, capped at a full persistent wave.
+    const long long need = (rows * 16 + kRopeThreads - 1) / kRopeThreads;
+    const unsigned blocks = (unsigned)std::min<long long>(need, (long long)sms[dev] * kRopeBlocksPerSm);
     switch (mode) {
         case kRopeOnly:
             rope_rows_kernel<kRopeOnly><<<blocks, kRopeThreads, 0, stream>>>(a);
