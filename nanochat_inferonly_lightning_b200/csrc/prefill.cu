@@ -173,19 +173,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && nb > 0) {
             const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
             const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
-            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+            // Descriptors are built once; a k-step only adds a constant to the start-address
+            // field (16-byte units): +2 per 32 bytes along K inside a 128-byte swizzled row,
+            // +1024 to move to the second 64-column box, +128 per 16 V rows (2048 bytes).
+            const uint64_t dQ = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), kBoxBytes, 1024);
+            constexpr uint64_t kStageStep = kTileBytes >> 4;
             auto issue_qk = [&](int j) -> bool {
                 const int st = j & 1;
                 if (!mbar_wait(&bars[kBarKFull + st], (j >> 1) & 1, abort_flag, p.status, 5))
                     return false;
                 tc_fence_after();
-                const uint32_t ak = aK + st * kTileBytes;
+                const uint64_t dK = dK0 + st * kStageStep;
                 const uint32_t ts = tmem + kColS + st * 128;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t koff = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                    mma_ss(ts, smem_desc_sw128(aQ + koff, 16, 1024),
-                           smem_desc_sw128(ak + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+                    const uint64_t ko = (kk >> 2) * 1024 + (kk & 3) * 2;
+                    mma_ss(ts, dQ + ko, dK + ko, idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&bars[kBarKFree + st]);
                 mma_commit(&bars[kBarS + st]);
@@ -200,14 +205,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6)) break;
                 if (!mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7)) break;
                 tc_fence_after();
-                const uint32_t av = aV + st * kTileBytes;
+                const uint64_t dV = dV0 + st * kStageStep;
                 const uint32_t tp = tmem + kColP + st * 64;
+                const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    // 16 keys per MMA: P columns [8kk, 8kk+8) (bf16 pairs), V rows
+                    // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
                     // [16kk, 16kk+16) = two 8-row swizzle groups.
-                    mma_ts(tmem + kColO, tp + kk * 8, smem_desc_sw128(av + kk * 2048, kBoxBytes, 1024),
-                           idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv, kk > 0 ? 1u : acc0);
                 }
                 mma_commit(&bars[kBarVFree + st]);
                 mma_commit(&bars[kBarPV + st]);
