@@ -74,6 +74,50 @@ __device__ __forceinline__ float exp2_poly(float x) {
     return __int_as_float(__float_as_int(p) + ((__float_as_int(r) - 0x4B400000) << 23));
 }
 
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic: one instruction, two lanes of work).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// exp2_poly on a packed pair (same method and coefficients); the clamp and the exponent
+// insertion are per element.  Because 0x4B400000 << 23 wraps to 0 in 32 bits, adding
+// (rounded << 23) to the polynomial's bits inserts the integer part directly.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+    x0 = fmaxf(x0, -127.0f);
+    x1 = fmaxf(x1, -127.0f);
+    const uint64_t x = f2_pack(x0, x1);
+    const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+    const uint64_t nmagic = f2_pack(-12582912.0f, -12582912.0f);
+    const uint64_t r = f2_add(x, magic);
+    const uint64_t n = f2_add(r, nmagic);
+    float n0, n1;
+    f2_unpack(n, n0, n1);
+    const uint64_t f = f2_add(x, f2_pack(-n0, -n1));
+    uint64_t q = f2_fma(f2_pack(0.05500893f, 0.05500893f), f, f2_pack(0.24221095f, 0.24221095f));
+    q = f2_fma(q, f, f2_pack(0.6932829f, 0.6932829f));
+    q = f2_fma(q, f, f2_pack(1.0f, 1.0f));
+    float q0, q1, r0, r1;
+    f2_unpack(q, q0, q1);
+    f2_unpack(r, r0, r1);
+    p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(r0) << 23));
+    p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(r1) << 23));
+}
+
 // RoPE (+ optional parameter-free RMSNorm) of one 128-wide head row held by a half-warp:
 // lane `sub` (0..15) owns dims [8*sub, 8*sub+8).  Half-split pairing (dim i with i+64,
 // reference kernels/rope.cu:95-97) puts a lane's partner at sub^8.  `mask` is the

@@ -248,21 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
             const int key0 = j * kBN;
-            if (key0 + kBN - 1 > q0 + off || key0 + kBN > kv_len) {
+            if (key0 + kBN - 1 > q0 + off || key0 + kBN > kv_len) {  // CTA-uniform branch
+                const int lim = min(qlim + 1, kv_len) - key0;  // columns >= lim are masked
 #pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int key = key0 + c;
-                    if (key > qlim || key >= kv_len) s[c] = kNegInf;
-                }
+                for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
             }
-            // Row max: eight independent partial maxima (short dependency chains).
+            // Row max: 3-input max over pairs, eight independent chains.
             float pm[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) pm[i] = s[i];
+            for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-            for (int c = 8; c < 128; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
-            const float bm = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+            for (int c = 16; c < 128; c += 2) pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
+            const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                                   fmaxf(pm[6], pm[7]));
             const float bm2 = bm * sl2;
             const bool renew = (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
             float alpha = 1.f;
@@ -291,20 +289,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
-            // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.
-            float ps[4] = {0.f, 0.f, 0.f, 0.f};
+            // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and the
+            // row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
+            // polynomial instead of MUFU.  Masked scores are -inf and give exactly 0.
+            const uint64_t sl2x2 = f2_pack(sl2, sl2);
+            const uint64_t nmu2 = f2_pack(-mu, -mu);
+            uint64_t acc2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
             uint32_t pk[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                // One pair in four goes through the FMA-pipe polynomial, the rest through MUFU.
-                const float x0 = __fmaf_rn(s[2 * i], sl2, -mu);
-                const float x1 = __fmaf_rn(s[2 * i + 1], sl2, -mu);
-                const bool poly = (i & 3) == 3;
-                const float p0 = poly ? exp2_poly(x0) : fast_exp2(x0);
-                const float p1 = poly ? exp2_poly(x1) : fast_exp2(x1);
-                ps[i & 3] += p0 + p1;
+                float x0, x1, p0, p1;
+                f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
+                if ((i & 3) == 3) {
+                    exp2_poly2(x0, x1, p0, p1);
+                } else {
+                    p0 = fast_exp2(x0);
+                    p1 = fast_exp2(x1);
+                }
+                acc2[i & 1] = f2_add(acc2[i & 1], f2_pack(p0, p1));
                 pk[i] = pack_bf16x2(p0, p1);
             }
+            float a0, a1, b0, b1;
+            f2_unpack(acc2[0], a0, a1);
+            f2_unpack(acc2[1], b0, b1);
+            const float rowsum = (a0 + a1) + (b0 + b1);
             // P(j & 1) was last read by PV(j-2); wait for it before overwriting.
             if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + st], ((j - 2) >> 1) & 1,
                                                              abort_flag, p.status, 12))) {
@@ -313,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
-            l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+            l += rowsum;
             tc_fence_before();
             mbar_arrive(&bars[kBarP + st]);
         }
