@@ -29,7 +29,8 @@ typedef enum nc_status {
     NC_ERR_CUDA = 3,            /* a CUDA runtime call failed (see nc_last_cuda_error)     */
     NC_ERR_WORKSPACE = 4,       /* workspace missing or smaller than required              */
     NC_ERR_RANGE = 5,           /* a position is beyond the RoPE table (20480 positions)   */
-    NC_ERR_DEVICE_TIMEOUT = 6   /* a kernel's bounded wait gave up (nc_device_status)      */
+    NC_ERR_DEVICE_TIMEOUT = 6,  /* a kernel's bounded wait gave up (nc_device_status)      */
+    NC_ERR_TOO_LARGE = 7        /* beyond the fixed scratch of nc_decode_attention_noalloc */
 } nc_status;
 
 /* Human-readable name of a status code. */
@@ -100,6 +101,22 @@ int nc_decode_attention(void* out, const void* q, const void* k_new, const void*
                         void* const* k_caches, void* const* v_caches, const int* kv_len,
                         int batch, int heads, float scale, int max_kv_len, int split_len,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* nc_decode_attention without the workspace argument, for callers that cannot allocate
+ * device memory (an engine whose device memory is planned by an outside allocator, a host
+ * binding with no device allocator to pass a workspace, or a latency-critical loop where
+ * cudaMalloc's device synchronization is not acceptable).  No counterpart in the reference:
+ * it is an addition of this library.  The split-KV partial results live in one fixed 8 MiB
+ * device array inside the library (held by every GPU that loads it until exit), so:
+ * batch <= 256 and max_kv_len <= 20480, else NC_ERR_TOO_LARGE; the split length grows as
+ * needed to fit.  All calls on a device share the array and it keeps the last call's
+ * contents: calls that overlap on the GPU race, so order them on one stream.  The first call
+ * on a device sets the array up (and, with k_new, uploads the RoPE table); make it before any
+ * stream capture.  Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+int nc_decode_attention_noalloc(void* out, const void* q, const void* k_new, const void* v_new,
+                                void* const* k_caches, void* const* v_caches, const int* kv_len,
+                                int batch, int heads, float scale, int max_kv_len,
+                                cudaStream_t stream);
 
 /* Batched causal prefill (chunked, with cache offset) for `batch` sequences whose caches
  * are slices of one slab: sequence b's rows start at k_slab + b * seq_stride elements

@@ -267,6 +267,10 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
 }
 
 }  // namespace
+
+int internal_rope_table(const float2** table) { return ensure_rope(table); }
+int internal_status_word(int** status) { return status_word(status); }
+
 }  // namespace nc
 
 using namespace nc;
@@ -285,6 +289,7 @@ const char* nc_status_string(int status) {
         case NC_ERR_WORKSPACE: return "workspace missing or too small";
         case NC_ERR_RANGE: return "position beyond the RoPE table";
         case NC_ERR_DEVICE_TIMEOUT: return "kernel wait timed out";
+        case NC_ERR_TOO_LARGE: return "request exceeds the fixed scratch of the allocation-free entry point";
         default: return "unknown status";
     }
 }

@@ -235,4 +235,10 @@ struct PrefillArgs {
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 
+// Host-side per-device state owned by api.cu, for other entry points of the library:
+// the RoPE table's device address (uploaded on first use) and the kernel status word.
+// Both return an nc_status.
+int internal_rope_table(const float2** table);
+int internal_status_word(int** status);
+
 }  // namespace nc
