@@ -4,12 +4,18 @@
 // Replaces the seq_q > 1 use of reference kernels/flash_attention.cu:19-171, which runs one
 // 128-thread CTA per (query, head) on CUDA cores and walks every key up to kv_len.
 //
-// Work unit: one CTA = 128 query rows x one head x one sequence.  Keys are consumed in
-// blocks of 128; only blocks that hold a visible key are visited (causal rule
+// Work unit ("tile"): 128 query rows x one head x one sequence.  Keys are consumed in blocks
+// of 128; only blocks that hold a visible key are visited (causal rule
 // key <= query + kv_offset and key < kv_len, reference flash_attention.cu:37, :74).
+// Persistent schedule: one CTA per SM walks a fixed list of tiles.  Tiles are ranked longest
+// first and dealt out in a zigzag (CTA c takes ranks c, 2G-1-c, 2G+c, ...), which evens out
+// the per-CTA sum of key blocks.  A running block counter drives every ring across tile
+// boundaries, and the Q tile is double-buffered, so the next tile's loads and first QK MMAs
+// overlap the current tile's last blocks and epilogue.
 //
 // Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: the Q tile once, then K(j) and V(j) into two-stage rings.
+//   warp 0      TMA producer: each tile's Q (two buffers), then K(j) and V(j) into two-stage
+//               rings.
 //   warp 1      allocates all 512 TMEM columns; one lane issues every tcgen05.mma.
 //   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
 // Tensor memory (512 columns): S0 [0,128) and S1 [128,256) hold Q.K^T of consecutive key
@@ -24,6 +30,8 @@
 // reference by more than 8 (log2 units).  Rows without any visible key produce NaN, as the
 // reference's 0/0 does.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "nc_common.cuh"
 #include "sm100_ptx.cuh"
@@ -45,8 +53,9 @@ constexpr float kRescaleThreshold = 8.0f;
 constexpr float kNegInf = -__builtin_huge_valf();
 
 enum Bar : int {
-    kBarQ = 0,
-    kBarKFull,   // [2]
+    kBarQ = 0,   // [2] Q buffer full
+    kBarQFree = kBarQ + 2,  // [2] every QK of the tile that used the Q buffer is done
+    kBarKFull = kBarQFree + 2,   // [2]
     kBarKFree = kBarKFull + 2,
     kBarVFull = kBarKFree + 2,
     kBarVFree = kBarVFull + 2,
@@ -63,8 +72,8 @@ struct __align__(8) SmemTail {
     int abort;
 };
 
-// Q tile + two K stages + two V stages.
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 5 * kTileBytes + sizeof(SmemTail);
+// Two Q buffers + two K stages + two V stages.
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 6 * kTileBytes + sizeof(SmemTail);
 
 struct PrefillKParams {
     bf16* out;
@@ -76,10 +85,69 @@ struct PrefillKParams {
     int seq_q;
     int heads;
     int n_qtiles;
-    int num_sms;
+    int total_tiles;
     float scale_log2;
     int* status;
 };
+
+// One tile of work: its coordinates and how many key blocks it visits.
+struct Tile {
+    int h, b, q0, off, kv_len, nb;
+};
+
+__device__ __forceinline__ Tile make_tile(const PrefillKParams& p, int rank) {
+    const int groups = p.heads * p.batch;
+    const int r = rank / groups;
+    const int g = rank - r * groups;
+    Tile t;
+    t.h = g % p.heads;
+    t.b = g / p.heads;
+    t.q0 = (p.n_qtiles - 1 - r) * kBM;  // rank 0 = last (longest) query tile
+    t.off = p.kv_offset_dev ? p.kv_offset_dev[t.b] : p.kv_offset;
+    t.kv_len = p.kv_len_from_offset ? t.off + p.seq_q : p.kv_len;
+    const int q_last = min(t.q0 + kBM - 1, p.seq_q - 1);
+    const int kv_end = min(t.kv_len, q_last + t.off + 1);  // keys [0, kv_end) may be visible
+    t.nb = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+    return t;
+}
+
+// Rank of the k-th tile of CTA c out of G: c, 2G-1-c, 2G+c, 4G-1-c, ...
+__device__ __forceinline__ int tile_rank(int k, int c, int G) {
+    const int base = (k >> 1) * 2 * G;
+    return (k & 1) ? base + 2 * G - 1 - c : base + c;
+}
+
+// Walks the key blocks of this CTA's non-empty tiles in order (used two blocks ahead by the
+// MMA issuer for its QK lookahead).
+struct BlockCursor {
+    int k, j, qi;  // tile index in the CTA's list, block in the tile, non-empty-tile counter
+    Tile t;
+    bool valid;
+};
+
+__device__ __forceinline__ void cursor_seek(BlockCursor& c, const PrefillKParams& p) {
+    // from tile index c.k (block 0), skip empty tiles
+    for (;; ++c.k) {
+        const int rank = tile_rank(c.k, blockIdx.x, gridDim.x);
+        if (rank >= p.total_tiles) {
+            c.valid = false;
+            return;
+        }
+        c.t = make_tile(p, rank);
+        if (c.t.nb > 0) {
+            c.j = 0;
+            c.valid = true;
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void cursor_next(BlockCursor& c, const PrefillKParams& p) {
+    if (++c.j < c.t.nb) return;
+    ++c.k;
+    ++c.qi;
+    cursor_seek(c, p);
+}
 
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* tmap, uint64_t* bar,
                                             int x, int y, int z) {
@@ -96,26 +164,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = smem + kTileBytes;       // stages at sK, sK + kTileBytes
-    uint8_t* sV = smem + 3 * kTileBytes;   // stages at sV, sV + kTileBytes
-    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 5 * kTileBytes);
+    uint8_t* sQ = smem;                    // buffers at sQ, sQ + kTileBytes
+    uint8_t* sK = smem + 2 * kTileBytes;   // stages at sK, sK + kTileBytes
+    uint8_t* sV = smem + 4 * kTileBytes;   // stages at sV, sV + kTileBytes
+    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 6 * kTileBytes);
     uint64_t* bars = tail->bars;
     volatile int* abort_flag = &tail->abort;
-
-    // Work order: longest query tiles first (the last tile of every (head, seq) group).
-    const int groups = p.heads * p.batch;
-    const int rank = blockIdx.x / groups;
-    const int g = blockIdx.x - rank * groups;
-    const int t = p.n_qtiles - 1 - rank;
-    const int h = g % p.heads;
-    const int b = g / p.heads;
-    const int q0 = t * kBM;
-    const int off = p.kv_offset_dev ? p.kv_offset_dev[b] : p.kv_offset;
-    const int kv_len = p.kv_len_from_offset ? off + p.seq_q : p.kv_len;
-    const int q_last = min(q0 + kBM - 1, p.seq_q - 1);
-    const int kv_end = min(kv_len, q_last + off + 1);  // keys [0, kv_end) may be visible
-    const int nb = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -140,51 +194,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
 
+    // Ring positions are driven by g, the running count of key blocks this CTA has visited
+    // (stage g & 1, parity (g >> 1) & 1), and by qi, the running count of non-empty tiles
+    // (Q buffer qi & 1, parity (qi >> 1) & 1).
     if (warp == 0) {
         // ------------------------------------------------------------------ producer
-        if (lane == 0 && nb > 0) {
-            const int x0 = h * 128;
-            mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
-            tma_load_3d(sQ, &tmQ, &bars[kBarQ], x0, q0, b);
-            tma_load_3d(sQ + kBoxBytes, &tmQ, &bars[kBarQ], x0 + 64, q0, b);
+        if (lane == 0) {
+            int g = 0, qi = 0;
             bool ok = true;
-            for (int j = 0; ok && j < nb; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = ((j >> 1) - 1) & 1;  // phase of the previous use of stage st
-                if (j >= 2 && !mbar_wait(&bars[kBarKFree + st], ph, abort_flag, p.status, 1)) break;
-                uint8_t* dk = sK + st * kTileBytes;
-                mbar_arrive_expect_tx(&bars[kBarKFull + st], kTileBytes);
-                tma_load_3d(dk, &tmK, &bars[kBarKFull + st], x0, j * kBN, b);
-                tma_load_3d(dk + kBoxBytes, &tmK, &bars[kBarKFull + st], x0 + 64, j * kBN, b);
-                if (j >= 2 && !mbar_wait(&bars[kBarVFree + st], ph, abort_flag, p.status, 2)) break;
-                uint8_t* dv = sV + st * kTileBytes;
-                mbar_arrive_expect_tx(&bars[kBarVFull + st], kTileBytes);
-                tma_load_3d(dv, &tmV, &bars[kBarVFull + st], x0, j * kBN, b);
-                tma_load_3d(dv + kBoxBytes, &tmV, &bars[kBarVFull + st], x0 + 64, j * kBN, b);
+            for (int k = 0; ok; ++k) {
+                const int rank = tile_rank(k, blockIdx.x, gridDim.x);
+                if (rank >= p.total_tiles) break;
+                const Tile t = make_tile(p, rank);
+                if (t.nb == 0) continue;
+                const int x0 = t.h * 128;
+                const int qb = qi & 1;
+                if (qi >= 2 &&
+                    !(ok = mbar_wait(&bars[kBarQFree + qb], ((qi >> 1) - 1) & 1, abort_flag, p.status, 1)))
+                    break;
+                uint8_t* dq = sQ + qb * kTileBytes;
+                mbar_arrive_expect_tx(&bars[kBarQ + qb], kTileBytes);
+                tma_load_3d(dq, &tmQ, &bars[kBarQ + qb], x0, t.q0, t.b);
+                tma_load_3d(dq + kBoxBytes, &tmQ, &bars[kBarQ + qb], x0 + 64, t.q0, t.b);
+                for (int j = 0; j < t.nb; ++j, ++g) {
+                    const int st = g & 1;
+                    const uint32_t ph = ((g >> 1) - 1) & 1;  // previous use of stage st
+                    if (g >= 2 && !(ok = mbar_wait(&bars[kBarKFree + st], ph, abort_flag, p.status, 2)))
+                        break;
+                    uint8_t* dk = sK + st * kTileBytes;
+                    mbar_arrive_expect_tx(&bars[kBarKFull + st], kTileBytes);
+                    tma_load_3d(dk, &tmK, &bars[kBarKFull + st], x0, j * kBN, t.b);
+                    tma_load_3d(dk + kBoxBytes, &tmK, &bars[kBarKFull + st], x0 + 64, j * kBN, t.b);
+                    if (g >= 2 && !(ok = mbar_wait(&bars[kBarVFree + st], ph, abort_flag, p.status, 3)))
+                        break;
+                    uint8_t* dv = sV + st * kTileBytes;
+                    mbar_arrive_expect_tx(&bars[kBarVFull + st], kTileBytes);
+                    tma_load_3d(dv, &tmV, &bars[kBarVFull + st], x0, j * kBN, t.b);
+                    tma_load_3d(dv + kBoxBytes, &tmV, &bars[kBarVFull + st], x0 + 64, j * kBN, t.b);
+                }
+                ++qi;
             }
-            // Do not leave the CTA with loads still landing in shared memory: the last V
-            // load of each stage is consumed by a PV whose completion arrives on kBarVFree.
-            for (int j = max(nb - 2, 0); j < nb; ++j)
-                mbar_wait(&bars[kBarVFree + (j & 1)], (j >> 1) & 1, abort_flag, p.status, 3);
+            // Do not leave with loads still landing in shared memory: every V load is
+            // consumed by a PV whose completion arrives on kBarVFree (the last two here).
+            for (int x = max(g - 2, 0); x < g; ++x)
+                mbar_wait(&bars[kBarVFree + (x & 1)], (x >> 1) & 1, abort_flag, p.status, 3);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
-        if (lane == 0 && nb > 0) {
+        if (lane == 0) {
             const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
             const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
             // Descriptors are built once; a k-step only adds a constant to the start-address
             // field (16-byte units): +2 per 32 bytes along K inside a 128-byte swizzled row,
             // +1024 to move to the second 64-column box, +128 per 16 V rows (2048 bytes).
-            const uint64_t dQ = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t dQ0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
             const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), kBoxBytes, 1024);
             constexpr uint64_t kStageStep = kTileBytes >> 4;
-            auto issue_qk = [&](int j) -> bool {
-                const int st = j & 1;
-                if (!mbar_wait(&bars[kBarKFull + st], (j >> 1) & 1, abort_flag, p.status, 5))
+            bool ok = true;
+            // QK runs two blocks ahead of PV: `ahead` is the block whose QK is next to issue,
+            // `ahead_g` its running block index.
+            BlockCursor ahead;
+            ahead.k = 0;
+            ahead.qi = 0;
+            cursor_seek(ahead, p);
+            int ahead_g = 0;
+            auto issue_qk = [&]() -> bool {
+                const int st = ahead_g & 1;
+                const int qb = ahead.qi & 1;
+                if (ahead.j == 0) {
+                    if (!mbar_wait(&bars[kBarQ + qb], (ahead.qi >> 1) & 1, abort_flag, p.status, 4))
+                        return false;
+                }
+                if (!mbar_wait(&bars[kBarKFull + st], (ahead_g >> 1) & 1, abort_flag, p.status, 5))
                     return false;
                 tc_fence_after();
+                const uint64_t dQ = dQ0 + qb * kStageStep;
                 const uint64_t dK = dK0 + st * kStageStep;
                 const uint32_t ts = tmem + kColS + st * 128;
 #pragma unroll
@@ -194,31 +280,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mma_commit(&bars[kBarKFree + st]);
                 mma_commit(&bars[kBarS + st]);
+                if (ahead.j + 1 == ahead.t.nb) mma_commit(&bars[kBarQFree + qb]);
+                cursor_next(ahead, p);
+                ++ahead_g;
                 return true;
             };
-            bool ok = mbar_wait(&bars[kBarQ], 0, abort_flag, p.status, 4);
-            ok = ok && issue_qk(0);
-            if (ok && nb > 1) ok = issue_qk(1);
-            for (int j = 0; ok && j < nb; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6)) break;
-                if (!mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7)) break;
-                tc_fence_after();
-                const uint64_t dV = dV0 + st * kStageStep;
-                const uint32_t tp = tmem + kColP + st * 64;
-                const uint32_t acc0 = j > 0 ? 1u : 0u;
+            if (ahead.valid) ok = issue_qk();
+            if (ok && ahead.valid) ok = issue_qk();
+            int g = 0;
+            for (int k = 0; ok; ++k) {
+                const int rank = tile_rank(k, blockIdx.x, gridDim.x);
+                if (rank >= p.total_tiles) break;
+                const Tile t = make_tile(p, rank);
+                for (int j = 0; ok && j < t.nb; ++j, ++g) {
+                    const int st = g & 1;
+                    const uint32_t ph = (g >> 1) & 1;
+                    if (!(ok = mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6))) break;
+                    if (!(ok = mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7))) break;
+                    tc_fence_after();
+                    const uint64_t dV = dV0 + st * kStageStep;
+                    const uint32_t tp = tmem + kColP + st * 64;
+                    const uint32_t acc0 = j > 0 ? 1u : 0u;  // first block of a tile starts O
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
-                    // [16kk, 16kk+16) = two 8-row swizzle groups.
-                    mma_ts(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv, kk > 0 ? 1u : acc0);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
+                        // [16kk, 16kk+16) = two 8-row swizzle groups.
+                        mma_ts(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
+                               kk > 0 ? 1u : acc0);
+                    }
+                    mma_commit(&bars[kBarVFree + st]);
+                    mma_commit(&bars[kBarPV + st]);
+                    if (j + 1 == t.nb) mma_commit(&bars[kBarOFinal]);
+                    // softmax(g) has read S(g & 1) (it wrote P(g) afterwards): refill it.
+                    if (ahead.valid) ok = issue_qk();
                 }
-                mma_commit(&bars[kBarVFree + st]);
-                mma_commit(&bars[kBarPV + st]);
-                if (j + 1 == nb) mma_commit(&bars[kBarOFinal]);
-                // softmax(j) has read S(j & 1) (it wrote P(j) afterwards): refill it.
-                if (j + 2 < nb) ok = issue_qk(j + 2);
             }
         }
         __syncwarp();
@@ -226,116 +321,129 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------ softmax / epilogue
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const int q = q0 + r;
-        const int qlim = q + off;  // last visible key for this row
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t tO = tmem + kColO + lane_base;
         const float sl2 = p.scale_log2;
-        float m_ref = kNegInf, l = 0.f;
+        int g = 0, qi = 0;
         bool ok = true;
-        for (int j = 0; j < nb; ++j) {
-            const int st = j & 1;
-            // Warp-uniform outcome: the TMEM accesses below are warp-collective.
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarS + st], (j >> 1) & 1, abort_flag,
-                                                   p.status, 9))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sraw[128];
-            tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
-            float s[128];
-#pragma unroll
-            for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
-            const int key0 = j * kBN;
-            if (key0 + kBN - 1 > q0 + off || key0 + kBN > kv_len) {  // CTA-uniform branch
-                const int lim = min(qlim + 1, kv_len) - key0;  // columns >= lim are masked
-#pragma unroll
-                for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
-            }
-            // Row max: 3-input max over pairs, eight independent chains.
-            float pm[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-            for (int c = 16; c < 128; c += 2) pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
-            const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
-                                   fmaxf(pm[6], pm[7]));
-            const float bm2 = bm * sl2;
-            const bool renew = (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
-            float alpha = 1.f;
-            if (renew) {
-                alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
-                m_ref = bm2;
-            }
-            l *= alpha;
-            // Rescale O for rows that renewed; O must first hold PV(j-1) complete.
-            if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
-                const int sp = (j - 1) & 1;
-                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + sp], ((j - 1) >> 1) & 1,
-                                                       abort_flag, p.status, 11))) {
+        for (int k = 0; ok; ++k) {
+            const int rank = tile_rank(k, blockIdx.x, gridDim.x);
+            if (rank >= p.total_tiles) break;
+            const Tile t = make_tile(p, rank);
+            const int q = t.q0 + r;
+            const int qlim = q + t.off;  // last visible key for this row
+            float m_ref = kNegInf, l = 0.f;
+            for (int j = 0; j < t.nb; ++j, ++g) {
+                const int st = g & 1;
+                // Warp-uniform outcome: the TMEM accesses below are warp-collective.
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarS + st], (g >> 1) & 1,
+                                                       abort_flag, p.status, 9))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                uint32_t sraw[128];
+                tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
+                float s[128];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t raw[32];
-                    tmem_ld32_sync(tO + 32 * c, raw);
+                for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
+                const int key0 = j * kBN;
+                if (key0 + kBN - 1 > t.q0 + t.off || key0 + kBN > t.kv_len) {  // CTA-uniform
+                    const int lim = min(qlim + 1, t.kv_len) - key0;  // columns >= lim masked
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
-                    tmem_st32_sync(tO + 32 * c, raw);
+                    for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
                 }
-            }
-            const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
-            // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and the
-            // row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
-            // polynomial instead of MUFU.  Masked scores are -inf and give exactly 0.
-            const uint64_t sl2x2 = f2_pack(sl2, sl2);
-            const uint64_t nmu2 = f2_pack(-mu, -mu);
-            uint64_t acc2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-            uint32_t pk[64];
+                // Row max: 3-input max over pairs, eight independent chains.
+                float pm[8];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                float x0, x1, p0, p1;
-                f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
-                if ((i & 3) == 3) {
-                    exp2_poly2(x0, x1, p0, p1);
-                } else {
-                    p0 = fast_exp2(x0);
-                    p1 = fast_exp2(x1);
+                for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+                for (int c = 16; c < 128; c += 2)
+                    pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
+                const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                                       fmaxf(pm[6], pm[7]));
+                const float bm2 = bm * sl2;
+                const bool renew =
+                    (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
+                float alpha = 1.f;
+                if (renew) {
+                    alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
+                    m_ref = bm2;
                 }
-                acc2[i & 1] = f2_add(acc2[i & 1], f2_pack(p0, p1));
-                pk[i] = pack_bf16x2(p0, p1);
+                l *= alpha;
+                // Rescale O for rows that renewed; O must first hold PV(g-1) complete.
+                if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
+                    const int sp = (g - 1) & 1;
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + sp], ((g - 1) >> 1) & 1,
+                                                           abort_flag, p.status, 11))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t raw[32];
+                        tmem_ld32_sync(tO + 32 * c, raw);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
+                        tmem_st32_sync(tO + 32 * c, raw);
+                    }
+                }
+                const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
+                // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and the
+                // row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
+                // polynomial instead of MUFU.  Masked scores are -inf and give exactly 0.
+                const uint64_t sl2x2 = f2_pack(sl2, sl2);
+                const uint64_t nmu2 = f2_pack(-mu, -mu);
+                uint64_t acc2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+                uint32_t pk[64];
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    float x0, x1, p0, p1;
+                    f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
+                    if ((i & 3) == 3) {
+                        exp2_poly2(x0, x1, p0, p1);
+                    } else {
+                        p0 = fast_exp2(x0);
+                        p1 = fast_exp2(x1);
+                    }
+                    acc2[i & 1] = f2_add(acc2[i & 1], f2_pack(p0, p1));
+                    pk[i] = pack_bf16x2(p0, p1);
+                }
+                float a0, a1, b0, b1;
+                f2_unpack(acc2[0], a0, a1);
+                f2_unpack(acc2[1], b0, b1);
+                // P(g & 1) was last read by PV(g-2); wait for it before overwriting.
+                if (g >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + st], ((g - 2) >> 1) & 1,
+                                                                 abort_flag, p.status, 12))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
+                l += (a0 + a1) + (b0 + b1);
+                tc_fence_before();
+                mbar_arrive(&bars[kBarP + st]);
             }
-            float a0, a1, b0, b1;
-            f2_unpack(acc2[0], a0, a1);
-            f2_unpack(acc2[1], b0, b1);
-            const float rowsum = (a0 + a1) + (b0 + b1);
-            // P(j & 1) was last read by PV(j-2); wait for it before overwriting.
-            if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + st], ((j - 2) >> 1) & 1,
-                                                             abort_flag, p.status, 12))) {
+            if (!ok) break;
+            // Epilogue: O / l -> bf16 -> out[b, q, h, :].  The next tile's first PV (which
+            // overwrites O) waits for that tile's P, written only after these reads finish.
+            bf16* orow = p.out + (((size_t)t.b * p.seq_q + q) * p.heads + t.h) * kHeadDim;
+            const bool store = q < p.seq_q;
+            if (t.nb == 0) {
+                if (store) {
+                    const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
+                }
+                continue;
+            }
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarOFinal], qi & 1, abort_flag, p.status, 10))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
-            l += rowsum;
-            tc_fence_before();
-            mbar_arrive(&bars[kBarP + st]);
-        }
-        // Epilogue: O / l -> bf16 -> out[b, q, h, :].
-        bf16* orow = p.out + (((size_t)b * p.seq_q + q) * p.heads + h) * kHeadDim;
-        const bool store = q < p.seq_q;
-        if (nb == 0) {
-            if (store) {
-                const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
-            }
-        } else if (ok && __all_sync(0xFFFFFFFFu,
-                                    mbar_wait(&bars[kBarOFinal], 0, abort_flag, p.status, 10))) {
+            ++qi;
             tc_fence_after();
             const float inv = 1.0f / l;  // l == 0 (no visible key) gives 0 * inf = NaN
 #pragma unroll
@@ -359,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            tc_fence_before();
         }
     }
 
@@ -446,11 +555,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         cudaError_t e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
     }
-    kp.num_sms = sm_count[dev];  // kept for schedulers that place work per SM
+    kp.total_tiles = kp.n_qtiles * a.heads * a.batch;
     kp.scale_log2 = a.scale * kLog2e;
     kp.status = a.status;
-    const long long nblocks = (long long)kp.n_qtiles * a.heads * a.batch;
-    prefill_kernel<<<(unsigned)nblocks, kThreads, kSmemBytes, stream>>>(mq, mk, mv, kp);
+    // Persistent: one CTA per SM (or fewer when there are fewer tiles).
+    const unsigned grid = (unsigned)std::min<long long>(kp.total_tiles, sm_count[dev]);
+    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, kp);
     return cudaGetLastError();
 }
 
