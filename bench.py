@@ -11,8 +11,10 @@ cfg3 (64 sequences, kv_len ~ U[1,2048], sharded over ranks), and chunked-prefill
 cfg4 (4 sequences x 512 queries at offset 1536, sharded over ranks).
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching
-stream; L2 is flushed (a 256 MiB write) and the step's in-place input restored before every
-step, outside the events.  Barrier + synchronize on both sides of the timed loop; the max over
+stream; L2 is flushed (a 256 MiB write, then a 256 MiB read that writes the dirty lines back)
+and the step's in-place input restored before every step, outside the events.  A decode
+workload whose per-rank inputs exceed twice the L2 (cfg3 on one GPU) runs its K steps back to
+back between two events instead, without flushing.  Barrier + synchronize on both sides of the timed loop; the max over
 ranks is reported.  `e2e` repeats the headline through the public API from pinned host
 buffers with the host->device copies of Q/K/V and the device->host copy of the output inside
 the timed region.
@@ -185,27 +187,54 @@ def stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-class Stepper:
-    """Runs W warm-up and K timed steps; each step may record sub-events (kernel splits)."""
+L2_BYTES = 126 << 20
 
-    def __init__(self, dist, flush):
+
+class Stepper:
+    """Runs W warm-up and K timed steps.
+
+    "flush" mode (inputs that fit in L2): before every step, outside the events, the step's
+    in-place inputs are restored, a 256 MiB buffer is written (evicting L2) and another 256 MiB
+    buffer is read (so the evicted dirty lines are written back before, not during, the timed
+    step); each step is bracketed by its own events and may record sub-events.
+    "stream" mode (inputs larger than 2x L2 per rank): the K steps run back to back between
+    two events, with no flush, and the mean is reported."""
+
+    def __init__(self, dist, flush, clean):
         self.dist = dist
         self.flush = flush
+        self.clean = clean
 
-    def run(self, step, K, Wm, restore=None, marks=0):
+    def _flush(self):
+        self.flush.zero_()
+        self.clean.sum(dtype=torch.int32)
+
+    def run(self, step, K, Wm, restore=None, marks=0, stream_mode=False):
         for _ in range(Wm):
             if restore:
                 restore()
-            self.flush.zero_()
+            if not stream_mode:
+                self._flush()
             step([])
         torch.cuda.synchronize()
         self.dist.barrier()
         torch.cuda.synchronize()
+        if stream_mode:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(K):
+                step([])
+            e1.record()
+            torch.cuda.synchronize()
+            self.dist.barrier()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / K
+            return [ms] * K, [[ms] * K]
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(marks + 2)] for _ in range(K)]
         for i in range(K):
             if restore:
                 restore()
-            self.flush.zero_()
+            self._flush()
             evs[i][0].record()
             step(evs[i][1:-1])
             evs[i][-1].record()
@@ -412,9 +441,11 @@ def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
                                                  ptr(vcs[i]), 1, L, H, float(W.SCALE), L - 1,
                                                  stream()) == 0
 
-        step_ms, _ = stepper.run(step, K, Wm)
+        stream_mode = bytes_rank > 2 * L2_BYTES
+        step_ms, _ = stepper.run(step, K, Wm, stream_mode=stream_mode)
         t_ms = sum(step_ms) / K
     else:
+        stream_mode = False
         stepper.run(lambda ev: None, K, Wm)
     t = dist.max(t_ms)
     total = dist.sum(bytes_rank)
@@ -423,6 +454,8 @@ def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
     return {
         "value": gbs, "unit": "GB/s", "ms_per_step": t, "sequences": len(lens_all),
         "bytes": W.decode_bytes(lens_all), "gpu_launches_per_step": launches,
+        "timing": ("back-to-back steps, inputs > 2x L2, no flush" if stream_mode else
+                   "per-step events, L2 flushed (write + read 256 MiB) before each step"),
         "roofline": {"bound": "hbm", "achieved": rank_gbs, "peak": peaks["hbm"], "unit": "GB/s",
                      "frac": rank_gbs / peaks["hbm"], "traffic": traffic.get(f"decode_kernel_{name}"),
                      "peak_src": peaks["src"]},
@@ -531,7 +564,8 @@ def main():
     peaks = load_peaks()
     traffic = load_traffic()
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-    stepper = Stepper(dist, flush)
+    clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
+    stepper = Stepper(dist, flush, clean)
 
     if args.only:
         fn = {"prefill": lambda: bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic, False),
@@ -575,7 +609,8 @@ def main():
             "workload": "cfg2: causal prefill, 1 sequence x 2048 positions per GPU, 17 heads x 128;"
                         " step = fused RoPE+QK-norm+KV-append pass + prefill attention",
             "seq_len": W.CFG2_SEQ, "heads": H, "head_dim": D, "sequences_per_gpu": 1,
-            "l2": "flushed before every timed step (256 MiB write); inputs restored outside the events",
+            "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read so the dirty "
+                  "lines are written back outside the events); inputs restored outside the events",
             "parallelism": f"replica x{args.gpus} (independent sequences, no collective)",
         },
         "attn_kernel_ms": head["attn_kernel_ms"],

@@ -24,7 +24,8 @@ extern "C" {
 
 typedef enum nc_status {
     NC_OK = 0,
-    NC_ERR_INVALID_ARG = 1,     /* bad size, null pointer, heads outside [1, 32] ...      */
+    NC_ERR_INVALID_ARG = 1,     /* bad size, null pointer, heads outside [1, 32] ([1, 31]
+                                   for the decode entry points) ...                        */
     NC_ERR_MISALIGNED = 2,      /* a pointer is not 16-byte aligned                        */
     NC_ERR_CUDA = 3,            /* a CUDA runtime call failed (see nc_last_cuda_error)     */
     NC_ERR_WORKSPACE = 4,       /* workspace missing or smaller than required              */

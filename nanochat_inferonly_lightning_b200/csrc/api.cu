@@ -102,7 +102,7 @@ WsLayout carve_ws(void* ws, int batch, int max_splits, int heads) {
     uint8_t* p = static_cast<uint8_t*>(ws);
     WsLayout w;
     w.counters = reinterpret_cast<unsigned*>(p);
-    size_t off = ((size_t)batch * sizeof(unsigned) + 255) & ~(size_t)255;
+    size_t off = (decode_counter_words(batch, heads) * sizeof(unsigned) + 255) & ~(size_t)255;
     w.part_ml = reinterpret_cast<float2*>(p + off);
     off = (off + n * sizeof(float2) + 255) & ~(size_t)255;
     w.part_o = reinterpret_cast<float*>(p + off);
@@ -138,7 +138,8 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
                   const int* kv_len, int n_visible_single, int batch, int heads, float scale,
                   int max_kv_len, int split_len, void* ws, size_t ws_bytes,
                   cudaStream_t stream) {
-    if (batch < 0 || check_heads(heads) || max_kv_len < 0) return NC_ERR_INVALID_ARG;
+    // The decode kernel runs one warp per head plus a producer warp (<= 1024 threads).
+    if (batch < 0 || heads < 1 || heads > 31 || max_kv_len < 0) return NC_ERR_INVALID_ARG;
     if (batch == 0) return NC_OK;
     if (!out || !q) return NC_ERR_INVALID_ARG;
     if ((k_new == nullptr) != (v_new == nullptr)) return NC_ERR_INVALID_ARG;

@@ -6,23 +6,58 @@
 // apply_rope_rmsnorm(q), apply_rope_rmsnorm(k) and the two cache-append copies of
 // src/model.cpp:119-131.
 //
-// Layout: K/V cache rows are [heads, 128] bf16 (4352 B for 17 heads).  Grid (split, seq):
-// each CTA owns `split_len` consecutive keys of one sequence and all heads; warp h = head h.
-// Inside a warp, lanes 0-15 take even keys and 16-31 odd keys; lane (sub = lane & 15) owns
-// dims [8*sub, 8*sub+8), so every load is a 16-byte vector and each half-warp reads one whole
-// 256-byte head row.  Eight keys per warp are in flight per iteration (4 K + 4 V loads per
-// lane).  Each half-warp keeps its own online-softmax state (max in log2 units, sum, 8
-// accumulators); the halves merge at the end, and splits merge through a small fp32
-// workspace in the last CTA of each sequence to finish (atomic ticket, self-resetting).
+// Work items are (sequence, split): `split_len` consecutive keys of one sequence, all heads.
+// The kernel is persistent (one CTA per SM).  Lane 0 of the last warp is the producer: it
+// pulls items from a global atomic counter and streams each item's K and V rows (a cache row
+// holds every head, heads*256 contiguous bytes, so R rows are one contiguous block) into a
+// three-stage shared-memory ring with bulk asynchronous copies (cp.async.bulk, completion on
+// an mbarrier).  The bytes in flight per SM are therefore set by the ring (three stages of
+// 2*R rows, ~200 KB), not by registers.  Warp h (< heads) consumes head h: half-warp 0 takes
+// even rows and half-warp 1 odd rows of each stage, lane `sub` reads dims [8*sub, 8*sub+8) of
+// its head with 16-byte shared-memory loads, and keeps an online softmax (max in log2 units,
+// sum, 8 fp32 accumulators).  At the end of an item the halves merge, and the split either
+// writes the output directly (single-split sequence) or a partial result; the last split of
+// each (sequence, head) to finish (per-head atomic ticket, self-resetting) combines them.
+#include <algorithm>
+
 #include "nc_common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace nc {
 
 namespace {
 
-constexpr int kUnroll = 4;  // keys per half-warp per iteration
+constexpr int kStages = 3;
 constexpr int kStatusDecodeBound = 0x200;  // a kv_len exceeded max_kv_len
 constexpr float kNegInf = -__builtin_huge_valf();
+constexpr int kQueueWords = 2;  // counters[0]: next work item; counters[1]: CTAs done fetching
+
+// Stage header, written by the producer before it arms the stage's full barrier.
+struct StageHdr {
+    int b;           // sequence, or -1: no more work
+    int first;       // first row of this stage (absolute key index)
+    int nrows;       // rows in this stage (0 for an item made of the new key only)
+    int item_first;  // 1 if this stage starts an item
+    int item_last;   // 1 if this stage ends an item
+    int split;
+    int n_splits;
+    int L;           // visible keys of the sequence
+};
+
+struct __align__(8) DecTail {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    StageHdr hdr[kStages];
+    int abort;
+};
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 
 __device__ __forceinline__ float dot8(const float (&q)[8], const uint4 kv) {
     float k[8];
@@ -33,249 +68,385 @@ __device__ __forceinline__ float dot8(const float (&q)[8], const uint4 kv) {
     return s;
 }
 
-__global__ void __launch_bounds__(1024) decode_kernel(DecodeArgs a) {
-    const int b = blockIdx.y;
-    const int split = blockIdx.x;
-    const int h = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int half = lane >> 4;
-    const int sub = lane & 15;
-    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+__device__ __forceinline__ int raw_len(const DecodeArgs& a, int b) {
+    return a.kv_len ? a.kv_len[b] : a.n_visible_single;
+}
+
+// MAX_THREADS selects the register budget: (heads + 1) warps must fit in it.
+template <int MAX_THREADS>
+__global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, int rows_per_stage) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
     const int H = a.heads;
-    const size_t rowstride = (size_t)H * kHeadDim;
+    const size_t rowstride = (size_t)H * kHeadDim;  // elements
+    const uint32_t rowbytes = (uint32_t)rowstride * 2;
+    const int R = rows_per_stage;
+    const uint32_t stage_bytes = 2u * R * rowbytes;  // K rows then V rows
+    DecTail* tail = reinterpret_cast<DecTail*>(smem + kStages * stage_bytes);
+    volatile int* abort_flag = &tail->abort;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
 
-    int L = a.kv_len ? a.kv_len[b] : a.n_visible_single;
-    bf16* out_row = a.out + (size_t)b * rowstride;
-    if (L <= 0) {
-        // No visible key: the reference's 0/0 yields NaN (flash_attention.cu:155).
-        if (split == 0 && half == 0) {
-            const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
-            *reinterpret_cast<uint4*>(out_row + h * kHeadDim + 8 * sub) = nan4;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&tail->full[s], 1);
+            mbar_init(&tail->empty[s], (uint32_t)H);
         }
-        return;
+        tail->abort = 0;
+        fence_mbar_init();
     }
-    if (L > a.max_kv_len) {
-        // kv_len[b] above the caller's bound (which sized the grid and the workspace): clamp,
-        // so no access leaves the promised rows, and flag it.
-        if (split == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusDecodeBound);
-        L = a.max_kv_len;
-    }
-    const int n_splits = (L + a.split_len - 1) / a.split_len;
-    if (split >= n_splits) return;
-    const int ks = split * a.split_len;
-    const int ke = min(L, ks + a.split_len);
-    const bool fuse_new = a.k_new != nullptr;
-    const bool owns_new = fuse_new && (split == n_splits - 1);
-    const int ke_stream = owns_new ? ke - 1 : ke;  // the new key is handled from registers
-
-    bf16* Kb = a.k_cache ? a.k_cache[b] : a.k_single;
-    bf16* Vb = a.v_cache ? a.v_cache[b] : a.v_single;
-    const size_t head_off = (size_t)h * kHeadDim + 8 * sub;
-    const int pos = L - 1;  // position of the query token
-
-    // Query: optional RoPE + QK-norm, rounded to bf16 like the unfused path, then
-    // pre-scaled so dot products come out in log2 units.
-    float qf[8];
-    {
-        const uint4 qr = *reinterpret_cast<const uint4*>(a.q + (size_t)b * rowstride + head_off);
-        if (a.q_raw) {
-            float y[8];
-            rope_norm_row(a.rope_cs, qr, sub, hmask, pos, true, y);
-            bf16x8_to_f32(f32_to_bf16x8(y), qf);
-        } else {
-            bf16x8_to_f32(qr, qf);
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) qf[e] *= a.scale_log2;
-    }
-
-    float m = kNegInf, l = 0.f, acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-
-    const bf16* kp = Kb + head_off;
-    const bf16* vp = Vb + head_off;
-    for (int k0 = ks; k0 < ke_stream; k0 += 2 * kUnroll) {
-        uint4 kr[kUnroll], vr[kUnroll];
-        bool valid[kUnroll];
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) {
-            const int key = k0 + 2 * i + half;
-            valid[i] = key < ke_stream;
-            kr[i] = valid[i] ? ldg_stream(kp + (size_t)key * rowstride) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) {
-            const int key = k0 + 2 * i + half;
-            vr[i] = valid[i] ? ldg_stream(vp + (size_t)key * rowstride) : make_uint4(0, 0, 0, 0);
-        }
-        float s[kUnroll];
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) s[i] = dot8(qf, kr[i]);
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) {
-            s[i] += __shfl_xor_sync(0xFFFFFFFFu, s[i], 8);
-            s[i] += __shfl_xor_sync(0xFFFFFFFFu, s[i], 4);
-            s[i] += __shfl_xor_sync(0xFFFFFFFFu, s[i], 2);
-            s[i] += __shfl_xor_sync(0xFFFFFFFFu, s[i], 1);
-            if (!valid[i]) s[i] = kNegInf;
-        }
-        float mx = s[0];
-#pragma unroll
-        for (int i = 1; i < kUnroll; ++i) mx = fmaxf(mx, s[i]);
-        const float m_new = fmaxf(m, mx);
-        const float mu = (m_new == kNegInf) ? 0.f : m_new;
-        const float alpha = fast_exp2(m - mu);
-        float p[kUnroll], psum = 0.f;
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) {
-            p[i] = fast_exp2(s[i] - mu);
-            psum += p[i];
-        }
-        l = __fmaf_rn(l, alpha, psum);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] *= alpha;
-#pragma unroll
-        for (int i = 0; i < kUnroll; ++i) {
-            float v[8];
-            bf16x8_to_f32(vr[i], v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(p[i], v[e], acc[e]);
-        }
-        m = m_new;
-    }
-
-    if (owns_new) {
-        // New token: RoPE + QK-norm of its key, append K and V to the cache, and add its
-        // contribution (lanes of half 0 only; half 1 contributes nothing for this key).
-        const size_t in_off = (size_t)b * rowstride + head_off;
-        const uint4 kr = *reinterpret_cast<const uint4*>(a.k_new + in_off);
-        const uint4 vr = *reinterpret_cast<const uint4*>(a.v_new + in_off);
-        float y[8];
-        rope_norm_row(a.rope_cs, kr, sub, hmask, pos, true, y);
-        const uint4 kn = f32_to_bf16x8(y);
-        if (half == 0) {
-            *reinterpret_cast<uint4*>(Kb + (size_t)pos * rowstride + head_off) = kn;
-            *reinterpret_cast<uint4*>(Vb + (size_t)pos * rowstride + head_off) = vr;
-        }
-        float s = dot8(qf, kn);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 8);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 4);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
-        if (half == 0) {
-            const float m_new = fmaxf(m, s);
-            const float alpha = fast_exp2(m - m_new);
-            const float p = fast_exp2(s - m_new);
-            l = __fmaf_rn(l, alpha, p);
-            float v[8];
-            bf16x8_to_f32(vr, v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(p, v[e], acc[e] * alpha);
-            m = m_new;
-        }
-    }
-
-    // Merge the two half-warps (same dims, disjoint keys).
-    {
-        const float m_o = __shfl_xor_sync(0xFFFFFFFFu, m, 16);
-        const float l_o = __shfl_xor_sync(0xFFFFFFFFu, l, 16);
-        const float M = fmaxf(m, m_o);
-        const float mu = (M == kNegInf) ? 0.f : M;
-        const float wa = fast_exp2(m - mu), wb = fast_exp2(m_o - mu);
-        l = l * wa + l_o * wb;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float o = __shfl_xor_sync(0xFFFFFFFFu, acc[e], 16);
-            acc[e] = acc[e] * wa + o * wb;
-        }
-        m = M;
-    }
-
-    if (n_splits == 1) {
-        if (half == 0) {
-            const float inv = 1.0f / l;
-            float o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = acc[e] * inv;
-            *reinterpret_cast<uint4*>(out_row + head_off) = f32_to_bf16x8(o);
-        }
-        return;
-    }
-
-    // Partial result of this split.
-    const size_t pidx = ((size_t)b * a.max_splits + split) * H + h;
-    if (half == 0) {
-        float4* po = reinterpret_cast<float4*>(a.part_o + pidx * kHeadDim + 8 * sub);
-        __stcg(po, make_float4(acc[0], acc[1], acc[2], acc[3]));
-        __stcg(po + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
-        if (sub == 0) __stcg(a.part_ml + pidx, make_float2(m, l));
-    }
-    __threadfence();
     __syncthreads();
-    __shared__ unsigned s_ticket;
-    if (threadIdx.x == 0) s_ticket = atomicAdd(a.counters + b, 1u);
-    __syncthreads();
-    if (s_ticket != (unsigned)(n_splits - 1)) return;
 
-    // Last CTA of this sequence: combine every split.  Warp h = head h; lanes read the
-    // split maxima in parallel, then each lane owns dims [4*lane, 4*lane+4) and keeps eight
-    // splits' partial rows in flight per round.
-    __threadfence();
-    if (threadIdx.x == 0) a.counters[b] = 0u;  // ready for the next launch
-    const size_t base = (size_t)b * a.max_splits * H + h;  // (b, split 0, h); split stride H
-    float M = kNegInf;
-    for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(a.part_ml + base + (size_t)sp * H).x);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-    const float mu = (M == kNegInf) ? 0.f : M;
-    float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
-        float2 ml[8];
-        float4 v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int sp = sp0 + i;
-            if (sp < n_splits) {
-                const size_t pi = base + (size_t)sp * H;
-                ml[i] = __ldcg(a.part_ml + pi);
-                v[i] = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * kHeadDim) + lane);
-            } else {
-                ml[i] = make_float2(kNegInf, 0.f);
-                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int total_items = a.max_splits * a.batch;  // split-major virtual items
+
+    if (warp == H) {
+        // -------------------------------------------------------------- producer
+        if (lane == 0) {
+            unsigned n = 0;  // stages armed by this CTA
+            bool ok = true;
+            // Slot of stage n; waits until the consumers released its previous use.
+            auto acquire_slot = [&](int& s) -> bool {
+                s = (int)(n % kStages);
+                const unsigned use = n / kStages;
+                return use == 0 ||
+                       mbar_wait(&tail->empty[s], (use - 1) & 1, abort_flag, a.status, 0x21);
+            };
+            for (;;) {
+                const int i = (int)atomicAdd(a.counters, 1u);
+                if (i >= total_items) break;
+                const int split = i / a.batch;
+                const int b = i - split * a.batch;
+                const int Lraw = raw_len(a, b);
+                const int L = min(Lraw, a.max_kv_len);
+                const int n_splits = L > 0 ? (L + a.split_len - 1) / a.split_len : 1;
+                if (split >= n_splits) continue;
+                if (split == 0 && Lraw > a.max_kv_len) atomicOr(a.status, kStatusDecodeBound);
+                const int ks = split * a.split_len;
+                const int ke = max(0, min(L, ks + a.split_len));
+                const bool owns_new = a.k_new != nullptr && L > 0 && ke == L;
+                const int ke_s = owns_new ? ke - 1 : ke;  // the new key comes from registers
+                const bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
+                const bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
+                for (int r0 = ks, first = 1; first || r0 < ke_s; r0 += R, first = 0) {
+                    const int nr = max(0, min(R, ke_s - r0));
+                    int s;
+                    if (!(ok = acquire_slot(s))) break;
+                    StageHdr& hd = tail->hdr[s];
+                    hd.b = b;
+                    hd.first = r0;
+                    hd.nrows = nr;
+                    hd.item_first = first;
+                    hd.item_last = (r0 + R >= ke_s) ? 1 : 0;
+                    hd.split = split;
+                    hd.n_splits = n_splits;
+                    hd.L = L;
+                    uint8_t* dst = smem + (size_t)s * stage_bytes;
+                    if (nr > 0) {
+                        mbar_arrive_expect_tx(&tail->full[s], 2u * nr * rowbytes);
+                        bulk_g2s(dst, kb + (size_t)r0 * rowstride, nr * rowbytes, &tail->full[s]);
+                        bulk_g2s(dst + (size_t)R * rowbytes, vb + (size_t)r0 * rowstride,
+                                 nr * rowbytes, &tail->full[s]);
+                    } else {
+                        mbar_arrive(&tail->full[s]);
+                    }
+                    ++n;
+                }
+                if (!ok) break;
+            }
+            // Tell the consumers there is no more work (one more stage, header b = -1).
+            int s;
+            if (ok && (ok = acquire_slot(s))) {
+                tail->hdr[s].b = -1;
+                mbar_arrive(&tail->full[s]);
+                ++n;
+            }
+            // Leave the queue ready for the next launch once every CTA has stopped fetching.
+            __threadfence();
+            if (atomicAdd(a.counters + 1, 1u) == gridDim.x - 1) {
+                a.counters[0] = 0u;
+                a.counters[1] = 0u;
+            }
+            // Do not leave with copies still landing: the data stages armed last are
+            // released by the consumers before they exit (the terminator is not released).
+            const unsigned data_stages = ok ? n - 1 : n;
+            for (unsigned x = 0; x < (unsigned)kStages && x < data_stages; ++x) {
+                const unsigned m_ = data_stages - 1 - x;
+                mbar_wait(&tail->empty[m_ % kStages], (m_ / kStages) & 1, abort_flag, a.status, 0x22);
             }
         }
+        __syncwarp();
+    } else if (warp < H) {
+        // -------------------------------------------------------------- consumers (head h)
+        const int h = warp;
+        const int half = lane >> 4;
+        const int sub = lane & 15;
+        const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+        const uint32_t head_off_b = (uint32_t)(h * kHeadDim + 8 * sub) * 2;  // bytes in a row
+        float qf[8], acc[8], m = kNegInf, l = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float w = fast_exp2(ml[i].x - mu);
-            den = __fmaf_rn(ml[i].y, w, den);
-            o4[0] = __fmaf_rn(v[i].x, w, o4[0]);
-            o4[1] = __fmaf_rn(v[i].y, w, o4[1]);
-            o4[2] = __fmaf_rn(v[i].z, w, o4[2]);
-            o4[3] = __fmaf_rn(v[i].w, w, o4[3]);
+        for (int e = 0; e < 8; ++e) qf[e] = acc[e] = 0.f;
+        unsigned n = 0;
+        for (;;) {
+            const int s = (int)(n % kStages);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&tail->full[s], (n / kStages) & 1, abort_flag,
+                                                   a.status, 0x23)))
+                break;
+            const StageHdr hd = tail->hdr[s];
+            if (hd.b < 0) break;
+            const int b = hd.b;
+            const size_t qoff = (size_t)b * rowstride + (size_t)h * kHeadDim + 8 * sub;
+            if (hd.item_first) {
+                m = kNegInf;
+                l = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+                const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
+                if (a.q_raw) {
+                    float y[8];
+                    rope_norm_row(a.rope_cs, qr, sub, hmask, max(hd.L - 1, 0), true, y);
+                    bf16x8_to_f32(f32_to_bf16x8(y), qf);  // bf16 like the unfused path
+                } else {
+                    bf16x8_to_f32(qr, qf);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) qf[e] *= a.scale_log2;
+            }
+            // Rows of this stage: half-warp `half` takes rows half, half + 2, ...
+            const uint8_t* sk = smem + (size_t)s * stage_bytes + head_off_b;
+            const uint8_t* sv = sk + (size_t)R * rowbytes;
+            // Operands come from shared memory (short latency), so two rows per half-warp per
+            // step are enough and keep the thread within 64 registers.
+            for (int r0 = 0; r0 < hd.nrows; r0 += 4) {
+                uint4 kr[2], vr[2];
+                bool valid[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int r = r0 + 2 * i + half;
+                    valid[i] = r < hd.nrows;
+                    const int rr = valid[i] ? r : 0;
+                    kr[i] = *reinterpret_cast<const uint4*>(sk + (size_t)rr * rowbytes);
+                    vr[i] = *reinterpret_cast<const uint4*>(sv + (size_t)rr * rowbytes);
+                }
+                float sc[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) sc[i] = dot8(qf, kr[i]);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 8);
+                    sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 4);
+                    sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 2);
+                    sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 1);
+                    if (!valid[i]) sc[i] = kNegInf;
+                }
+                const float m_new = fmaxf(m, fmaxf(sc[0], sc[1]));
+                const float mu = (m_new == kNegInf) ? 0.f : m_new;
+                const float alpha = fast_exp2(m - mu);
+                const float p0 = fast_exp2(sc[0] - mu), p1 = fast_exp2(sc[1] - mu);
+                l = __fmaf_rn(l, alpha, p0 + p1);
+                float v0[8], v1[8];
+                bf16x8_to_f32(vr[0], v0);
+                bf16x8_to_f32(vr[1], v1);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    acc[e] = __fmaf_rn(p1, v1[e], __fmaf_rn(p0, v0[e], acc[e] * alpha));
+                m = m_new;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tail->empty[s]);
+            ++n;
+            if (!hd.item_last) continue;
+
+            // ---- end of item
+            const int L = hd.L;
+            bf16* out_row = a.out + (size_t)b * rowstride + (size_t)h * kHeadDim;
+            if (L <= 0) {
+                // No visible key: the reference's 0/0 yields NaN (flash_attention.cu:155).
+                if (half == 0)
+                    *reinterpret_cast<uint4*>(out_row + 8 * sub) =
+                        make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+                continue;
+            }
+            const int ks = hd.split * a.split_len;
+            const int ke = min(L, ks + a.split_len);
+            if (a.k_new != nullptr && ke == L) {
+                // New token (position L-1): RoPE + QK-norm of its key, append K and V to the
+                // cache, add its contribution (lanes of half 0 only).
+                const int pos = L - 1;
+                bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
+                bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
+                const uint4 kr = *reinterpret_cast<const uint4*>(a.k_new + qoff);
+                const uint4 vr = *reinterpret_cast<const uint4*>(a.v_new + qoff);
+                float y[8];
+                rope_norm_row(a.rope_cs, kr, sub, hmask, pos, true, y);
+                const uint4 kn = f32_to_bf16x8(y);
+                const size_t coff = (size_t)pos * rowstride + (size_t)h * kHeadDim + 8 * sub;
+                if (half == 0) {
+                    *reinterpret_cast<uint4*>(kb + coff) = kn;
+                    *reinterpret_cast<uint4*>(vb + coff) = vr;
+                }
+                float sc = dot8(qf, kn);
+                sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 8);
+                sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 4);
+                sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 2);
+                sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 1);
+                if (half == 0) {
+                    const float m_new = fmaxf(m, sc);
+                    const float alpha = fast_exp2(m - m_new);
+                    const float pr = fast_exp2(sc - m_new);
+                    l = __fmaf_rn(l, alpha, pr);
+                    float v[8];
+                    bf16x8_to_f32(vr, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(pr, v[e], acc[e] * alpha);
+                    m = m_new;
+                }
+            }
+            // Merge the two half-warps (same dims, disjoint keys).
+            {
+                const float m_o = __shfl_xor_sync(0xFFFFFFFFu, m, 16);
+                const float l_o = __shfl_xor_sync(0xFFFFFFFFu, l, 16);
+                const float M = fmaxf(m, m_o);
+                const float mu = (M == kNegInf) ? 0.f : M;
+                const float wa = fast_exp2(m - mu), wb = fast_exp2(m_o - mu);
+                l = l * wa + l_o * wb;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float o = __shfl_xor_sync(0xFFFFFFFFu, acc[e], 16);
+                    acc[e] = acc[e] * wa + o * wb;
+                }
+                m = M;
+            }
+            if (hd.n_splits == 1) {
+                if (half == 0) {
+                    const float inv = 1.0f / l;
+                    float o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[e] = acc[e] * inv;
+                    *reinterpret_cast<uint4*>(out_row + 8 * sub) = f32_to_bf16x8(o);
+                }
+                continue;
+            }
+            // Partial result of this split, then the per-(sequence, head) ticket.
+            const size_t pidx = ((size_t)b * a.max_splits + hd.split) * H + h;
+            if (half == 0) {
+                float4* po = reinterpret_cast<float4*>(a.part_o + pidx * kHeadDim + 8 * sub);
+                __stcg(po, make_float4(acc[0], acc[1], acc[2], acc[3]));
+                __stcg(po + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
+                if (sub == 0) __stcg(a.part_ml + pidx, make_float2(m, l));
+            }
+            __threadfence();
+            __syncwarp();
+            unsigned ticket = 0;
+            unsigned* ctr = a.counters + kQueueWords + (size_t)b * H + h;
+            if (lane == 0) ticket = atomicAdd(ctr, 1u);
+            ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+            if (ticket != (unsigned)(hd.n_splits - 1)) continue;
+            // Last split of (b, h): combine.  Lane owns dims [4*lane, 4*lane+4).
+            __threadfence();
+            if (lane == 0) *ctr = 0u;  // ready for the next launch
+            const size_t base = (size_t)b * a.max_splits * H + h;
+            float M = kNegInf;
+            for (int sp = lane; sp < hd.n_splits; sp += 32)
+                M = fmaxf(M, __ldcg(a.part_ml + base + (size_t)sp * H).x);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+            const float mu = (M == kNegInf) ? 0.f : M;
+            float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int sp0 = 0; sp0 < hd.n_splits; sp0 += 4) {
+                float2 ml[4];
+                float4 v[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int sp = sp0 + i;
+                    if (sp < hd.n_splits) {
+                        const size_t pi = base + (size_t)sp * H;
+                        ml[i] = __ldcg(a.part_ml + pi);
+                        v[i] = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * kHeadDim) + lane);
+                    } else {
+                        ml[i] = make_float2(kNegInf, 0.f);
+                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float w = fast_exp2(ml[i].x - mu);
+                    den = __fmaf_rn(ml[i].y, w, den);
+                    o4[0] = __fmaf_rn(v[i].x, w, o4[0]);
+                    o4[1] = __fmaf_rn(v[i].y, w, o4[1]);
+                    o4[2] = __fmaf_rn(v[i].z, w, o4[2]);
+                    o4[3] = __fmaf_rn(v[i].w, w, o4[3]);
+                }
+            }
+            const float inv = 1.0f / den;
+            uint2 r;
+            r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
+            r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
+            *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
         }
     }
-    const float inv = 1.0f / den;
-    uint2 r;
-    r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
-    r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
-    *reinterpret_cast<uint2*>(out_row + (size_t)h * kHeadDim + 4 * lane) = r;
+    __syncthreads();
 }
 
 }  // namespace
 
+// Rows per ring stage for a head count: three stages of K and V rows within ~216 KB.
+int decode_rows_per_stage(int heads) {
+    const int rowbytes = heads * kHeadDim * 2;
+    int r = (216 * 1024) / (kStages * 2 * rowbytes);
+    r = std::min(r, 16) & ~1;
+    return std::max(r, 2);
+}
+
+size_t decode_smem_bytes(int heads) {
+    const size_t rowbytes = (size_t)heads * kHeadDim * 2;
+    return 128 + (size_t)kStages * 2 * decode_rows_per_stage(heads) * rowbytes + sizeof(DecTail);
+}
+
+size_t decode_counter_words(int batch, int heads) {
+    return kQueueWords + (size_t)batch * heads;
+}
+
 size_t decode_workspace_bytes(int batch, int max_splits, int heads) {
     const size_t n = (size_t)batch * max_splits * heads;
-    size_t bytes = ((size_t)batch * sizeof(unsigned) + 255) & ~(size_t)255;  // counters
-    bytes = (bytes + n * sizeof(float2) + 255) & ~(size_t)255;                 // part_ml
-    bytes += n * kHeadDim * sizeof(float);                                     // part_o
+    size_t bytes = (decode_counter_words(batch, heads) * sizeof(unsigned) + 255) & ~(size_t)255;
+    bytes = (bytes + n * sizeof(float2) + 255) & ~(size_t)255;  // part_ml
+    bytes += n * kHeadDim * sizeof(float);                      // part_o
     return (bytes + 255) & ~(size_t)255;
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     if (a.batch <= 0) return cudaSuccess;
-    dim3 grid(a.max_splits, a.batch);
-    decode_kernel<<<grid, a.heads * 32, 0, stream>>>(a);
+    static int sms[64] = {};
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!sms[dev]) {
+        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    if (!attr[dev]) {
+        size_t most = 0;  // the opt-in must cover every head count the kernel accepts
+        for (int hh = 1; hh <= 31; ++hh) most = std::max(most, decode_smem_bytes(hh));
+        e = cudaFuncSetAttribute(decode_kernel<576>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)most);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_kernel<1024>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    const long long items = (long long)a.max_splits * a.batch;
+    const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(items, sms[dev]));
+    const int threads = (a.heads + 1) * 32;  // one warp per head + the producer warp
+    if (threads <= 576)
+        decode_kernel<576><<<grid, threads, decode_smem_bytes(a.heads), stream>>>(
+            a, decode_rows_per_stage(a.heads));
+    else
+        decode_kernel<1024><<<grid, threads, decode_smem_bytes(a.heads), stream>>>(
+            a, decode_rows_per_stage(a.heads));
     return cudaGetLastError();
 }
 

@@ -30,10 +30,12 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = 8u << 20;
 constexpr int kNoAllocMaxBatch = 256;
-constexpr size_t kCounterBytes = kNoAllocMaxBatch * sizeof(unsigned);  // fixed, offset 0
+// Work-queue words and per-(sequence, head) split tickets for batch 256 x 32 heads (32.8 KB),
+// at a fixed offset 0.
+constexpr size_t kCounterBytes = 64u << 10;
 constexpr int kMaxDevices = 64;
 
-// Split counters at [0, 1 KiB), then the partial maxima/sums and the partial accumulators.
+// Split counters at [0, 64 KiB), then the partial maxima/sums and the partial accumulators.
 // Zero at module load; the decode kernel leaves every counter at zero when it finishes.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -81,7 +83,7 @@ extern "C" int nc_decode_attention_noalloc(void* out, const void* q, const void*
                                            void* const* v_caches, const int* kv_len, int batch,
                                            int heads, float scale, int max_kv_len,
                                            cudaStream_t stream) {
-    if (batch < 0 || heads < 1 || heads > 32 || max_kv_len < 0) return NC_ERR_INVALID_ARG;
+    if (batch < 0 || heads < 1 || heads > 31 || max_kv_len < 0) return NC_ERR_INVALID_ARG;
     if (batch == 0) return NC_OK;
     if (!out || !q || !k_caches || !v_caches || !kv_len) return NC_ERR_INVALID_ARG;
     if ((k_new == nullptr) != (v_new == nullptr)) return NC_ERR_INVALID_ARG;

@@ -209,12 +209,15 @@ struct DecodeArgs {
     int max_splits;
     float* part_o;                // [B, max_splits, heads, 128]
     float2* part_ml;              // [B, max_splits, heads]
-    unsigned* counters;           // [B], zero between launches
+    unsigned* counters;           // decode_counter_words(B, heads), zero between launches
     int* status;                  // device status word (argument violations seen on device)
 };
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
 size_t decode_workspace_bytes(int batch, int max_splits, int heads);
+// 32-bit words at the start of the decode workspace: two work-queue words, then one split
+// ticket per (sequence, head).  All zero between launches.
+size_t decode_counter_words(int batch, int heads);
 
 struct PrefillArgs {
     bf16* out;                    // [B, seq_q, heads*128]

@@ -14,8 +14,8 @@
 // overlap the current tile's last blocks and epilogue.
 //
 // Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: each tile's Q (two buffers), then K(j) and V(j) into two-stage
-//               rings.
+//   warp 0      TMA producers: lane 0 each tile's Q (two buffers) and K(j) into a two-stage
+//               ring, lane 1 V(j) into a two-stage ring.
 //   warp 1      allocates all 512 TMEM columns; one lane issues every tcgen05.mma.
 //   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
 // Tensor memory (512 columns): S0 [0,128) and S1 [128,256) hold Q.K^T of consecutive key
@@ -32,6 +32,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "nc_common.cuh"
 #include "sm100_ptx.cuh"
@@ -56,12 +57,10 @@ enum Bar : int {
     kBarQ = 0,   // [2] Q buffer full
     kBarQFree = kBarQ + 2,  // [2] every QK of the tile that used the Q buffer is done
     kBarKFull = kBarQFree + 2,   // [2]
-    kBarKFree = kBarKFull + 2,
-    kBarVFull = kBarKFree + 2,
-    kBarVFree = kBarVFull + 2,
-    kBarS = kBarVFree + 2,
-    kBarP = kBarS + 2,
-    kBarPV = kBarP + 2,
+    kBarVFull = kBarKFull + 2,   // [2]
+    kBarS = kBarVFull + 2,       // [2] QK(g) done: S(g & 1) full and K stage g & 1 free
+    kBarP = kBarS + 2,           // [2] softmax wrote P(g)
+    kBarPV = kBarP + 2,          // [2] PV(g) done: V stage free, P(g & 1) free
     kBarOFinal = kBarPV + 2,
     kNumBars
 };
@@ -198,8 +197,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (stage g & 1, parity (g >> 1) & 1), and by qi, the running count of non-empty tiles
     // (Q buffer qi & 1, parity (qi >> 1) & 1).
     if (warp == 0) {
-        // ------------------------------------------------------------------ producer
-        if (lane == 0) {
+        // ------------------------------------------------------------------ producers
+        // Lane 0 loads Q and K, lane 1 loads V, each waiting only on the barrier that frees
+        // its own ring, so K(g+2) streams in as soon as QK(g) is done, independently of V.
+        if (lane < 2) {
+            const bool kq = lane == 0;
             int g = 0, qi = 0;
             bool ok = true;
             for (int k = 0; ok; ++k) {
@@ -208,36 +210,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const Tile t = make_tile(p, rank);
                 if (t.nb == 0) continue;
                 const int x0 = t.h * 128;
-                const int qb = qi & 1;
-                if (qi >= 2 &&
-                    !(ok = mbar_wait(&bars[kBarQFree + qb], ((qi >> 1) - 1) & 1, abort_flag, p.status, 1)))
-                    break;
-                uint8_t* dq = sQ + qb * kTileBytes;
-                mbar_arrive_expect_tx(&bars[kBarQ + qb], kTileBytes);
-                tma_load_3d(dq, &tmQ, &bars[kBarQ + qb], x0, t.q0, t.b);
-                tma_load_3d(dq + kBoxBytes, &tmQ, &bars[kBarQ + qb], x0 + 64, t.q0, t.b);
+                if (kq) {
+                    const int qb = qi & 1;
+                    if (qi >= 2 && !(ok = mbar_wait(&bars[kBarQFree + qb], ((qi >> 1) - 1) & 1,
+                                                    abort_flag, p.status, 1)))
+                        break;
+                    uint8_t* dq = sQ + qb * kTileBytes;
+                    mbar_arrive_expect_tx(&bars[kBarQ + qb], kTileBytes);
+                    tma_load_3d(dq, &tmQ, &bars[kBarQ + qb], x0, t.q0, t.b);
+                    tma_load_3d(dq + kBoxBytes, &tmQ, &bars[kBarQ + qb], x0 + 64, t.q0, t.b);
+                }
                 for (int j = 0; j < t.nb; ++j, ++g) {
                     const int st = g & 1;
                     const uint32_t ph = ((g >> 1) - 1) & 1;  // previous use of stage st
-                    if (g >= 2 && !(ok = mbar_wait(&bars[kBarKFree + st], ph, abort_flag, p.status, 2)))
+                    // K stage st is free once QK(g-2) completed (kBarS), V stage once PV(g-2) did.
+                    if (g >= 2 && !(ok = mbar_wait(&bars[(kq ? kBarS : kBarPV) + st], ph, abort_flag,
+                                                   p.status, kq ? 2 : 3)))
                         break;
-                    uint8_t* dk = sK + st * kTileBytes;
-                    mbar_arrive_expect_tx(&bars[kBarKFull + st], kTileBytes);
-                    tma_load_3d(dk, &tmK, &bars[kBarKFull + st], x0, j * kBN, t.b);
-                    tma_load_3d(dk + kBoxBytes, &tmK, &bars[kBarKFull + st], x0 + 64, j * kBN, t.b);
-                    if (g >= 2 && !(ok = mbar_wait(&bars[kBarVFree + st], ph, abort_flag, p.status, 3)))
-                        break;
-                    uint8_t* dv = sV + st * kTileBytes;
-                    mbar_arrive_expect_tx(&bars[kBarVFull + st], kTileBytes);
-                    tma_load_3d(dv, &tmV, &bars[kBarVFull + st], x0, j * kBN, t.b);
-                    tma_load_3d(dv + kBoxBytes, &tmV, &bars[kBarVFull + st], x0 + 64, j * kBN, t.b);
+                    uint8_t* dst = (kq ? sK : sV) + st * kTileBytes;
+                    uint64_t* full = &bars[(kq ? kBarKFull : kBarVFull) + st];
+                    const CUtensorMap* map = kq ? &tmK : &tmV;
+                    mbar_arrive_expect_tx(full, kTileBytes);
+                    tma_load_3d(dst, map, full, x0, j * kBN, t.b);
+                    tma_load_3d(dst + kBoxBytes, map, full, x0 + 64, j * kBN, t.b);
                 }
                 ++qi;
             }
-            // Do not leave with loads still landing in shared memory: every V load is
-            // consumed by a PV whose completion arrives on kBarVFree (the last two here).
+            // Do not leave with loads still landing in shared memory: the last loads of each
+            // ring are consumed by MMAs whose completion arrives on kBarS (K) / kBarPV (V).
             for (int x = max(g - 2, 0); x < g; ++x)
-                mbar_wait(&bars[kBarVFree + (x & 1)], (x >> 1) & 1, abort_flag, p.status, 3);
+                mbar_wait(&bars[(kq ? kBarS : kBarPV) + (x & 1)], (x >> 1) & 1, abort_flag, p.status, 3);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -253,50 +255,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), kBoxBytes, 1024);
             constexpr uint64_t kStageStep = kTileBytes >> 4;
             bool ok = true;
-            // QK runs two blocks ahead of PV: `ahead` is the block whose QK is next to issue,
-            // `ahead_g` its running block index.
-            BlockCursor ahead;
+            // The tensor pipe's instruction queue is shallow, so any work of this thread between
+            // MMAs shows up as tensor idle time.  Each block therefore runs one straight
+            // sequence: wait for P(g), V(g) and the operands of QK(g+2); issue the 8 P.V MMAs
+            // and the 8 Q.K^T MMAs back to back; then two commits (kBarPV also frees V stage
+            // g & 1, kBarS also frees the K stage).  QK stays two blocks ahead of PV.
+            BlockCursor ahead;  // the block whose QK is next to issue
             ahead.k = 0;
             ahead.qi = 0;
             cursor_seek(ahead, p);
             int ahead_g = 0;
-            auto issue_qk = [&]() -> bool {
-                const int st = ahead_g & 1;
-                const int qb = ahead.qi & 1;
-                if (ahead.j == 0) {
-                    if (!mbar_wait(&bars[kBarQ + qb], (ahead.qi >> 1) & 1, abort_flag, p.status, 4))
-                        return false;
-                }
-                if (!mbar_wait(&bars[kBarKFull + st], (ahead_g >> 1) & 1, abort_flag, p.status, 5))
+            auto wait_qk_operands = [&]() -> bool {
+                if (ahead.j == 0 &&
+                    !mbar_wait(&bars[kBarQ + (ahead.qi & 1)], (ahead.qi >> 1) & 1, abort_flag, p.status, 4))
                     return false;
-                tc_fence_after();
-                const uint64_t dQ = dQ0 + qb * kStageStep;
-                const uint64_t dK = dK0 + st * kStageStep;
-                const uint32_t ts = tmem + kColS + st * 128;
+                return mbar_wait(&bars[kBarKFull + (ahead_g & 1)], (ahead_g >> 1) & 1, abort_flag,
+                                 p.status, 5);
+            };
+            auto issue_qk = [&]() {
+                const uint64_t dQ = dQ0 + (ahead.qi & 1) * kStageStep;
+                const uint64_t dK = dK0 + (ahead_g & 1) * kStageStep;
+                const uint32_t ts = tmem + kColS + (ahead_g & 1) * 128;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t ko = (kk >> 2) * 1024 + (kk & 3) * 2;
                     mma_ss(ts, dQ + ko, dK + ko, idesc_qk, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&bars[kBarKFree + st]);
-                mma_commit(&bars[kBarS + st]);
-                if (ahead.j + 1 == ahead.t.nb) mma_commit(&bars[kBarQFree + qb]);
+            };
+            auto commit_qk = [&]() {
+                mma_commit(&bars[kBarS + (ahead_g & 1)]);
+                if (ahead.j + 1 == ahead.t.nb) mma_commit(&bars[kBarQFree + (ahead.qi & 1)]);
                 cursor_next(ahead, p);
                 ++ahead_g;
-                return true;
             };
-            if (ahead.valid) ok = issue_qk();
-            if (ok && ahead.valid) ok = issue_qk();
+            // Prologue: QK of the first two blocks.
+            for (int i = 0; i < 2 && ok && ahead.valid; ++i) {
+                if (!(ok = wait_qk_operands())) break;
+                tc_fence_after();
+                issue_qk();
+                commit_qk();
+            }
             int g = 0;
             for (int k = 0; ok; ++k) {
                 const int rank = tile_rank(k, blockIdx.x, gridDim.x);
                 if (rank >= p.total_tiles) break;
-                const Tile t = make_tile(p, rank);
-                for (int j = 0; ok && j < t.nb; ++j, ++g) {
+                const int nb = make_tile(p, rank).nb;
+                for (int j = 0; ok && j < nb; ++j, ++g) {
                     const int st = g & 1;
                     const uint32_t ph = (g >> 1) & 1;
+                    const bool next = ahead.valid;
                     if (!(ok = mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6))) break;
                     if (!(ok = mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7))) break;
+                    if (next && !(ok = wait_qk_operands())) break;
                     tc_fence_after();
                     const uint64_t dV = dV0 + st * kStageStep;
                     const uint32_t tp = tmem + kColP + st * 64;
@@ -308,11 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mma_ts(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
                                kk > 0 ? 1u : acc0);
                     }
-                    mma_commit(&bars[kBarVFree + st]);
+                    if (next) issue_qk();
+                    // softmax(g) has read S(g & 1) (it wrote P(g) afterwards), so QK(g+2) may
+                    // refill it; kBarPV(g) completes after PV(g) (and QK(g+2), issued before).
                     mma_commit(&bars[kBarPV + st]);
-                    if (j + 1 == t.nb) mma_commit(&bars[kBarOFinal]);
-                    // softmax(g) has read S(g & 1) (it wrote P(g) afterwards): refill it.
-                    if (ahead.valid) ok = issue_qk();
+                    if (j + 1 == nb) mma_commit(&bars[kBarOFinal]);
+                    if (next) commit_qk();
                 }
             }
         }
@@ -517,6 +528,48 @@ bool make_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
            CUDA_SUCCESS;
 }
 
+// Encoded tensor maps are cached per device (keyed by every encoding parameter), so repeated
+// calls on the same buffers, e.g. one per layer and decode step of an engine, skip the host
+// encoding work.  Small direct-mapped table; a collision just re-encodes.
+struct MapKey {
+    const void* base;
+    int heads, rows, batch, dev;
+    long long stride;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && heads == o.heads && rows == o.rows && batch == o.batch &&
+               dev == o.dev && stride == o.stride;
+    }
+};
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+std::mutex g_map_mutex;
+MapEntry g_maps[256];
+
+bool cached_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
+                long long batch_stride_elems, int dev) {
+    const MapKey key{base, heads, rows, batch, dev, batch_stride_elems};
+    size_t h = reinterpret_cast<uintptr_t>(base) >> 8;
+    h ^= (size_t)rows * 0x9E3779B1u ^ (size_t)heads * 0x85EBCA6Bu ^ (size_t)batch * 0xC2B2AE35u ^
+         (size_t)dev * 0x27D4EB2Fu ^ (size_t)batch_stride_elems;
+    MapEntry& e = g_maps[h & 255];
+    {
+        std::lock_guard<std::mutex> lk(g_map_mutex);
+        if (e.used && e.key == key) {
+            *m = e.map;
+            return true;
+        }
+    }
+    if (!make_map(m, base, heads, rows, batch, batch_stride_elems)) return false;
+    std::lock_guard<std::mutex> lk(g_map_mutex);
+    e.key = key;
+    e.map = *m;
+    e.used = true;
+    return true;
+}
+
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
@@ -536,9 +589,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     }
     CUtensorMap mq, mk, mv;
     const int kv_rows = a.kv_rows;
-    if (!make_map(&mq, a.q, a.heads, a.seq_q, a.batch, (long long)a.seq_q * a.heads * 128) ||
-        !make_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride) ||
-        !make_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride))
+    if (!cached_map(&mq, a.q, a.heads, a.seq_q, a.batch, (long long)a.seq_q * a.heads * 128, dev) ||
+        !cached_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev) ||
+        !cached_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev))
         return cudaErrorInvalidValue;
     PrefillKParams kp;
     kp.out = a.out;
