@@ -188,6 +188,11 @@ def stream():
 
 
 L2_BYTES = 126 << 20
+# A GPU-side spin (torch's _sleep kernel, ~50 us) queued just before each start event holds
+# the stream while the host enqueues the step, so the events bracket the step's device
+# execution and not the host's launch latency (the blocking-kernel method of nvbench).  The
+# e2e figure, which goes through the host API with host buffers, includes the host cost.
+HOLD_CYCLES = 100_000
 
 
 class Stepper:
@@ -196,7 +201,8 @@ class Stepper:
     "flush" mode (inputs that fit in L2): before every step, outside the events, the step's
     in-place inputs are restored, a 256 MiB buffer is written (evicting L2) and another 256 MiB
     buffer is read (so the evicted dirty lines are written back before, not during, the timed
-    step); each step is bracketed by its own events and may record sub-events.
+    step), then the hold spin is queued; each step is bracketed by its own events and may
+    record sub-events.
     "stream" mode (inputs larger than 2x L2 per rank): the K steps run back to back between
     two events, with no flush, and the mean is reported."""
 
@@ -221,6 +227,7 @@ class Stepper:
         torch.cuda.synchronize()
         if stream_mode:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(HOLD_CYCLES)
             e0.record()
             for _ in range(K):
                 step([])
@@ -235,6 +242,7 @@ class Stepper:
             if restore:
                 restore()
             self._flush()
+            torch.cuda._sleep(HOLD_CYCLES)
             evs[i][0].record()
             step(evs[i][1:-1])
             evs[i][-1].record()
@@ -611,6 +619,8 @@ def main():
             "seq_len": W.CFG2_SEQ, "heads": H, "head_dim": D, "sequences_per_gpu": 1,
             "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read so the dirty "
                   "lines are written back outside the events); inputs restored outside the events",
+            "timing": "CUDA events per step on the launching stream, behind a ~50 us GPU-side hold "
+                      "spin so that host launch latency is not counted (e2e counts it)",
             "parallelism": f"replica x{args.gpus} (independent sequences, no collective)",
         },
         "attn_kernel_ms": head["attn_kernel_ms"],

@@ -244,90 +244,94 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
-            const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
-            // Descriptors are built once; a k-step only adds a constant to the start-address
-            // field (16-byte units): +2 per 32 bytes along K inside a 128-byte swizzled row,
-            // +1024 to move to the second 64-column box, +128 per 16 V rows (2048 bytes).
-            const uint64_t dQ0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
-            const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
-            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), kBoxBytes, 1024);
-            constexpr uint64_t kStageStep = kTileBytes >> 4;
-            bool ok = true;
-            // The tensor pipe's instruction queue is shallow, so any work of this thread between
-            // MMAs shows up as tensor idle time.  Each block therefore runs one straight
-            // sequence: wait for P(g), V(g) and the operands of QK(g+2); issue the 8 P.V MMAs
-            // and the 8 Q.K^T MMAs back to back; then two commits (kBarPV also frees V stage
-            // g & 1, kBarS also frees the K stage).  QK stays two blocks ahead of PV.
-            BlockCursor ahead;  // the block whose QK is next to issue
-            ahead.k = 0;
-            ahead.qi = 0;
-            cursor_seek(ahead, p);
-            int ahead_g = 0;
-            auto wait_qk_operands = [&]() -> bool {
-                if (ahead.j == 0 &&
-                    !mbar_wait(&bars[kBarQ + (ahead.qi & 1)], (ahead.qi >> 1) & 1, abort_flag, p.status, 4))
-                    return false;
-                return mbar_wait(&bars[kBarKFull + (ahead_g & 1)], (ahead_g >> 1) & 1, abort_flag,
-                                 p.status, 5);
-            };
-            auto issue_qk = [&]() {
-                const uint64_t dQ = dQ0 + (ahead.qi & 1) * kStageStep;
-                const uint64_t dK = dK0 + (ahead_g & 1) * kStageStep;
-                const uint32_t ts = tmem + kColS + (ahead_g & 1) * 128;
+        // The whole warp runs this loop, converged, so the descriptors and the loop state
+        // stay in uniform registers; every MMA and commit is issued by one elected lane
+        // (the same lane each time).  Each wait is taken by all lanes and combined with a
+        // vote so that control flow stays uniform.
+        const uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false);  // B = K tile, K-major
+        const uint32_t idesc_pv = idesc_bf16_f32(kBM, 128, true);   // B = V tile, MN-major
+        // Descriptors are built once; a k-step only adds a constant to the start-address
+        // field (16-byte units): +2 per 32 bytes along K inside a 128-byte swizzled row,
+        // +1024 to move to the second 64-column box, +128 per 16 V rows (2048 bytes).
+        const uint64_t dQ0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+        const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+        const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), kBoxBytes, 1024);
+        constexpr uint64_t kStageStep = kTileBytes >> 4;
+        auto wait_all = [&](int bar, uint32_t parity, int tag) -> bool {
+            return __all_sync(0xFFFFFFFFu,
+                              mbar_wait(&bars[bar], parity, abort_flag, p.status, tag));
+        };
+        bool ok = true;
+        // Per block: wait for V(g) and P(g); issue the 8 P.V MMAs; wait for the operands of
+        // QK(g+2); issue its 8 Q.K^T MMAs and commit kBarS (frees the K stage and hands S to
+        // the softmax); then commit kBarPV (frees V stage g & 1 and P(g & 1)).  QK stays two
+        // blocks ahead of PV.
+        BlockCursor ahead;  // the block whose QK is next to issue
+        ahead.k = 0;
+        ahead.qi = 0;
+        cursor_seek(ahead, p);
+        int ahead_g = 0;
+        auto wait_qk_operands = [&]() -> bool {
+            if (ahead.j == 0 && !wait_all(kBarQ + (ahead.qi & 1), (ahead.qi >> 1) & 1, 4))
+                return false;
+            return wait_all(kBarKFull + (ahead_g & 1), (ahead_g >> 1) & 1, 5);
+        };
+        auto issue_qk = [&]() {
+            const uint64_t dQ = dQ0 + (ahead.qi & 1) * kStageStep;
+            const uint64_t dK = dK0 + (ahead_g & 1) * kStageStep;
+            const uint32_t ts = tmem + kColS + (ahead_g & 1) * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t ko = (kk >> 2) * 1024 + (kk & 3) * 2;
+                mma_ss_warp(ts, dQ + ko, dK + ko, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            mma_commit_warp(&bars[kBarS + (ahead_g & 1)]);
+            if (ahead.j + 1 == ahead.t.nb) mma_commit_warp(&bars[kBarQFree + (ahead.qi & 1)]);
+            cursor_next(ahead, p);
+            ++ahead_g;
+        };
+        // Prologue: QK of the first two blocks.
+        for (int i = 0; i < 2 && ok && ahead.valid; ++i) {
+            if (!(ok = wait_qk_operands())) break;
+            tc_fence_after();
+            issue_qk();
+        }
+        int g = 0;
+        for (int k = 0; ok; ++k) {
+            const int rank = tile_rank(k, blockIdx.x, gridDim.x);
+            if (rank >= p.total_tiles) break;
+            const int nb = make_tile(p, rank).nb;
+            for (int j = 0; ok && j < nb; ++j, ++g) {
+                const int st = g & 1;
+                const uint32_t ph = (g >> 1) & 1;
+                if (!(ok = wait_all(kBarVFull + st, ph, 7))) break;
+                if (!(ok = wait_all(kBarP + st, ph, 6))) break;
+                tc_fence_after();
+                const uint64_t dV = dV0 + st * kStageStep;
+                const uint32_t tp = tmem + kColP + st * 64;
+                const uint32_t acc0 = j > 0 ? 1u : 0u;  // first block of a tile starts O
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t ko = (kk >> 2) * 1024 + (kk & 3) * 2;
-                    mma_ss(ts, dQ + ko, dK + ko, idesc_qk, kk > 0 ? 1u : 0u);
+                    // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
+                    // [16kk, 16kk+16) = two 8-row swizzle groups.
+                    mma_ts_warp(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
+                                kk > 0 ? 1u : acc0);
                 }
-            };
-            auto commit_qk = [&]() {
-                mma_commit(&bars[kBarS + (ahead_g & 1)]);
-                if (ahead.j + 1 == ahead.t.nb) mma_commit(&bars[kBarQFree + (ahead.qi & 1)]);
-                cursor_next(ahead, p);
-                ++ahead_g;
-            };
-            // Prologue: QK of the first two blocks.
-            for (int i = 0; i < 2 && ok && ahead.valid; ++i) {
-                if (!(ok = wait_qk_operands())) break;
-                tc_fence_after();
-                issue_qk();
-                commit_qk();
-            }
-            int g = 0;
-            for (int k = 0; ok; ++k) {
-                const int rank = tile_rank(k, blockIdx.x, gridDim.x);
-                if (rank >= p.total_tiles) break;
-                const int nb = make_tile(p, rank).nb;
-                for (int j = 0; ok && j < nb; ++j, ++g) {
-                    const int st = g & 1;
-                    const uint32_t ph = (g >> 1) & 1;
-                    const bool next = ahead.valid;
-                    if (!(ok = mbar_wait(&bars[kBarP + st], ph, abort_flag, p.status, 6))) break;
-                    if (!(ok = mbar_wait(&bars[kBarVFull + st], ph, abort_flag, p.status, 7))) break;
-                    if (next && !(ok = wait_qk_operands())) break;
+                // softmax(g) has read S(g & 1) (it wrote P(g) afterwards), so QK(g+2) may
+                // refill it.
+                if (ahead.valid) {
+                    if (!(ok = wait_qk_operands())) break;
                     tc_fence_after();
-                    const uint64_t dV = dV0 + st * kStageStep;
-                    const uint32_t tp = tmem + kColP + st * 64;
-                    const uint32_t acc0 = j > 0 ? 1u : 0u;  // first block of a tile starts O
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
-                        // [16kk, 16kk+16) = two 8-row swizzle groups.
-                        mma_ts(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
-                               kk > 0 ? 1u : acc0);
-                    }
-                    if (next) issue_qk();
-                    // softmax(g) has read S(g & 1) (it wrote P(g) afterwards), so QK(g+2) may
-                    // refill it; kBarPV(g) completes after PV(g) (and QK(g+2), issued before).
-                    mma_commit(&bars[kBarPV + st]);
-                    if (j + 1 == nb) mma_commit(&bars[kBarOFinal]);
-                    if (next) commit_qk();
+                    issue_qk();
                 }
+                // Committed after QK(g+2): completes once PV(g) and QK(g+2) are done.  Freeing
+                // V stage g & 1 this late keeps the V reload off the tensor pipe's critical
+                // stretch (measured: committing right after the P.V MMAs made the next QK
+                // batch ~4x slower).
+                mma_commit_warp(&bars[kBarPV + st]);
+                if (j + 1 == nb) mma_commit_warp(&bars[kBarOFinal]);
             }
         }
-        __syncwarp();
     } else {
         // ------------------------------------------------------------------ softmax / epilogue
         const int quarter = warp & 3;
