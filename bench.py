@@ -188,11 +188,11 @@ def stream():
 
 
 L2_BYTES = 126 << 20
-# A GPU-side spin (torch's _sleep kernel, ~50 us) queued just before each start event holds
+# A GPU-side spin (torch's _sleep kernel, ~0.5 ms) queued just before each start event holds
 # the stream while the host enqueues the step, so the events bracket the step's device
 # execution and not the host's launch latency (the blocking-kernel method of nvbench).  The
 # e2e figure, which goes through the host API with host buffers, includes the host cost.
-HOLD_CYCLES = 100_000
+HOLD_CYCLES = 1_000_000
 
 
 class Stepper:
@@ -619,7 +619,7 @@ def main():
             "seq_len": W.CFG2_SEQ, "heads": H, "head_dim": D, "sequences_per_gpu": 1,
             "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read so the dirty "
                   "lines are written back outside the events); inputs restored outside the events",
-            "timing": "CUDA events per step on the launching stream, behind a ~50 us GPU-side hold "
+            "timing": "CUDA events per step on the launching stream, behind a ~0.5 ms GPU-side hold "
                       "spin so that host launch latency is not counted (e2e counts it)",
             "parallelism": f"replica x{args.gpus} (independent sequences, no collective)",
         },

@@ -429,13 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float a0, a1, b0, b1;
                 f2_unpack(acc2[0], a0, a1);
                 f2_unpack(acc2[1], b0, b1);
-                // P(g & 1) was last read by PV(g-2); wait for it before overwriting.
-                if (g >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + st], ((g - 2) >> 1) & 1,
-                                                                 abort_flag, p.status, 12))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                // P(g & 1) was last read by PV(g-2).  No wait is needed: the MMA thread issued
+                // QK(g) after PV(g-2) and committed kBarS(g) after both, and a commit completes
+                // only when every earlier MMA of the issuing thread has, so the kBarS(g) wait
+                // above already covers PV(g-2).
                 tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
                 l += (a0 + a1) + (b0 + b1);
                 tc_fence_before();

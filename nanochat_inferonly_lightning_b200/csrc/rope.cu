@@ -5,9 +5,11 @@
 // rope_rmsnorm_kernel/apply_rope_rmsnorm :74-158) and the two cudaMemcpyAsync cache appends
 // in src/model.cpp:122-131.
 //
-// Mapping: one half-warp per (position, head) row, 16 lanes x 16-byte loads = one 256-byte
-// head row, so a warp moves two full rows per instruction (fully coalesced).  The pair
-// partner (dim i <-> i+64) sits eight lanes away and is fetched with one shuffle per word.
+// Mapping: eight lanes per (position, head) row.  Lane s owns the rotation pairs
+// (i, i + 64) for i in [8s, 8s + 8): it loads dims [8s, 8s + 8) and [64 + 8s, 64 + 8s + 8)
+// with two 16-byte loads, so the rotation needs no data from other lanes and the 128-dim
+// RMS norm is a three-step butterfly over the row's eight lanes.  A warp covers four rows
+// per instruction; each row half is one contiguous 128-byte segment (coalesced).
 #include <algorithm>
 #include <cmath>
 #include <mutex>
@@ -22,57 +24,137 @@ namespace {
 // cos/sin table (10.5 MB per device), filled by upload_rope_table().
 __device__ float2 g_rope_cs[kRopeMaxSeq * kHalfDim];
 
-constexpr int kRopeThreads = 256;  // 16 half-warps per block
-constexpr int kRopeBlocksPerSm = 4;
+constexpr int kRopeThreads = 256;  // 32 rows per block
 
-// One (position, head) row's inputs for one lane: 16 bytes of q (or x), k and v.
+// One row's inputs for one lane: the low and high 16-byte slices of q (or x), k and v, and
+// the lane's eight (cos, sin) pairs of the row's position.
 struct RowIn {
-    uint4 q, k, v;
+    uint4 qlo, qhi, klo, khi, vlo, vhi;
+    float4 cs[4];
 };
 
 template <int MODE>
-__device__ __forceinline__ RowIn load_row(const RopeArgs& a, size_t off) {
+__device__ __forceinline__ RowIn load_row(const RopeArgs& a, size_t off, int pos, int s8) {
     RowIn r;
-    r.q = __ldcs(reinterpret_cast<const uint4*>(a.q + off));
+    const float4* cs = reinterpret_cast<const float4*>(a.rope_cs + (size_t)pos * kHalfDim + 8 * s8);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.cs[i] = __ldg(cs + i);
+    r.qlo = __ldcs(reinterpret_cast<const uint4*>(a.q + off));
+    r.qhi = __ldcs(reinterpret_cast<const uint4*>(a.q + off + 64));
     if (MODE == kRopeNormAppend) {
-        r.k = __ldcs(reinterpret_cast<const uint4*>(a.k + off));
-        r.v = __ldcs(reinterpret_cast<const uint4*>(a.v + off));
+        r.klo = __ldcs(reinterpret_cast<const uint4*>(a.k + off));
+        r.khi = __ldcs(reinterpret_cast<const uint4*>(a.k + off + 64));
+        r.vlo = __ldcs(reinterpret_cast<const uint4*>(a.v + off));
+        r.vhi = __ldcs(reinterpret_cast<const uint4*>(a.v + off + 64));
     }
     return r;
 }
 
-// Persistent, grid-stride streaming pass: each half-warp walks rows row, row + stride, ...
-// and issues the loads of its next row before it computes the current one, so every lane
-// keeps two rows of loads in flight.
+// RoPE (+ optional RMS norm) of one lane's 16 values.  Same per-element arithmetic as the
+// reference (kernels/rope.cu:105-107, :137): y_lo = x_lo*c + x_hi*s, y_hi = x_hi*c - x_lo*s,
+// then y * rsqrt(mean(y^2) + 1e-6), the sum of squares taken as two 8-term fma chains (low
+// and high dims) added, then a butterfly over the row's eight lanes (`gmask`).
+__device__ __forceinline__ void rope_norm_pairs(const float4 (&cs)[4], uint4 lo, uint4 hi,
+                                                unsigned gmask, bool norm, uint4& out_lo,
+                                                uint4& out_hi) {
+    float xl[8], xh[8];
+    bf16x8_to_f32(lo, xl);
+    bf16x8_to_f32(hi, xh);
+    float c[8], sn[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 t = cs[i];
+        c[2 * i] = t.x;
+        sn[2 * i] = t.y;
+        c[2 * i + 1] = t.z;
+        sn[2 * i + 1] = t.w;
+    }
+    float yl[8], yh[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        yl[e] = __fmaf_rn(xl[e], c[e], xh[e] * sn[e]);
+        yh[e] = __fmaf_rn(xh[e], c[e], -(xl[e] * sn[e]));
+    }
+    if (norm) {
+        float sl = 0.f, sh = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            sl = __fmaf_rn(yl[e], yl[e], sl);
+            sh = __fmaf_rn(yh[e], yh[e], sh);
+        }
+        float ss = sl + sh;
+        ss += __shfl_xor_sync(gmask, ss, 4);
+        ss += __shfl_xor_sync(gmask, ss, 2);
+        ss += __shfl_xor_sync(gmask, ss, 1);
+        const float r = rsqrtf(ss * (1.0f / kHeadDim) + kNormEps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            yl[e] *= r;
+            yh[e] *= r;
+        }
+    }
+    out_lo = f32_to_bf16x8(yl);
+    out_hi = f32_to_bf16x8(yh);
+}
+
+// Persistent, grid-stride streaming pass: each 8-lane group walks rows row, row + stride,
+// ... and issues the loads of its next row (data and cos/sin) before it computes the
+// current one.  Raw inputs
+// are read with evict-first loads; outputs use ordinary stores so that they stay in L2 for
+// the attention kernel that reads them next.
 template <int MODE>
 __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
-    const int hw = (blockIdx.x * kRopeThreads + threadIdx.x) >> 4;
-    const int stride = (gridDim.x * kRopeThreads) >> 4;
-    const int sub = threadIdx.x & 15;
-    const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
+    const int grp = (blockIdx.x * kRopeThreads + threadIdx.x) >> 3;
+    const int stride = (gridDim.x * kRopeThreads) >> 3;
+    const int s8 = threadIdx.x & 7;
+    const unsigned gmask = 0xFFu << (threadIdx.x & 24);
     const int nrows = a.seq_len * a.heads;
-    int row = hw;
-    if (row >= nrows) return;  // whole half-warps leave together
-    RowIn cur = load_row<MODE>(a, (size_t)row * kHeadDim + 8 * sub);
+    int row = grp;
+    if (row >= nrows) return;  // whole 8-lane groups leave together
+    RowIn cur = load_row<MODE>(a, (size_t)row * kHeadDim + 8 * s8, a.start_pos + row / a.heads, s8);
     for (; row < nrows; row += stride) {
         const int next = row + stride;
         RowIn nxt;
-        if (next < nrows) nxt = load_row<MODE>(a, (size_t)next * kHeadDim + 8 * sub);
-        const size_t off = (size_t)row * kHeadDim + 8 * sub;
-        const int pos = a.start_pos + row / a.heads;
-        float y[8];
+        if (next < nrows)
+            nxt = load_row<MODE>(a, (size_t)next * kHeadDim + 8 * s8, a.start_pos + next / a.heads, s8);
+        const size_t off = (size_t)row * kHeadDim + 8 * s8;
+        uint4 ol, oh;
         if (MODE == kRopeNormAppend) {
-            rope_norm_row(a.rope_cs, cur.q, sub, mask, pos, true, y);
-            __stcs(reinterpret_cast<uint4*>(a.q + off), f32_to_bf16x8(y));
-            rope_norm_row(a.rope_cs, cur.k, sub, mask, pos, true, y);
-            *reinterpret_cast<uint4*>(a.k_dst + off) = f32_to_bf16x8(y);
-            *reinterpret_cast<uint4*>(a.v_dst + off) = cur.v;
+            rope_norm_pairs(cur.cs, cur.qlo, cur.qhi, gmask, true, ol, oh);
+            *reinterpret_cast<uint4*>(a.q + off) = ol;
+            *reinterpret_cast<uint4*>(a.q + off + 64) = oh;
+            rope_norm_pairs(cur.cs, cur.klo, cur.khi, gmask, true, ol, oh);
+            *reinterpret_cast<uint4*>(a.k_dst + off) = ol;
+            *reinterpret_cast<uint4*>(a.k_dst + off + 64) = oh;
+            *reinterpret_cast<uint4*>(a.v_dst + off) = cur.vlo;
+            *reinterpret_cast<uint4*>(a.v_dst + off + 64) = cur.vhi;
         } else {
-            rope_norm_row(a.rope_cs, cur.q, sub, mask, pos, MODE == kRopeNorm, y);
-            *reinterpret_cast<uint4*>(a.q + off) = f32_to_bf16x8(y);
+            rope_norm_pairs(cur.cs, cur.qlo, cur.qhi, gmask, MODE == kRopeNorm, ol, oh);
+            *reinterpret_cast<uint4*>(a.q + off) = ol;
+            *reinterpret_cast<uint4*>(a.q + off + 64) = oh;
         }
         cur = nxt;
     }
+}
+
+template <int MODE>
+cudaError_t launch_rope_mode(const RopeArgs& a, long long rows, int dev, cudaStream_t stream) {
+    // Persistent wave: as many blocks as are resident at once on the device (occupancy
+    // queried once per device), or fewer when there are fewer rows.
+    static int wave[64] = {};
+    if (!wave[dev]) {
+        int sms = 0, per_sm = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rope_rows_kernel<MODE>,
+                                                          kRopeThreads, 0);
+        if (e != cudaSuccess) return e;
+        wave[dev] = sms * std::max(per_sm, 1);
+    }
+    const long long need = (rows * 8 + kRopeThreads - 1) / kRopeThreads;
+    const unsigned blocks = (unsigned)std::min<long long>(need, wave[dev]);
+    rope_rows_kernel<MODE><<<blocks, kRopeThreads, 0, stream>>>(a);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -80,30 +162,16 @@ __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
 cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream) {
     const long long rows = (long long)a.seq_len * a.heads;
     if (rows <= 0) return cudaSuccess;
-    static int sms[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!sms[dev]) {
-        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-    }
-    // Enough half-warps for every row, capped at a full persistent wave.
-    const long long need = (rows * 16 + kRopeThreads - 1) / kRopeThreads;
-    const unsigned blocks = (unsigned)std::min<long long>(need, (long long)sms[dev] * kRopeBlocksPerSm);
     switch (mode) {
-        case kRopeOnly:
-            rope_rows_kernel<kRopeOnly><<<blocks, kRopeThreads, 0, stream>>>(a);
-            break;
-        case kRopeNorm:
-            rope_rows_kernel<kRopeNorm><<<blocks, kRopeThreads, 0, stream>>>(a);
-            break;
-        case kRopeNormAppend:
-            rope_rows_kernel<kRopeNormAppend><<<blocks, kRopeThreads, 0, stream>>>(a);
-            break;
+        case kRopeOnly: return launch_rope_mode<kRopeOnly>(a, rows, dev, stream);
+        case kRopeNorm: return launch_rope_mode<kRopeNorm>(a, rows, dev, stream);
+        case kRopeNormAppend: return launch_rope_mode<kRopeNormAppend>(a, rows, dev, stream);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
 }
 
 // Host-side table, computed once per process with the same fp32 libm calls and the same
