@@ -128,8 +128,13 @@ def reference_kernels():
         lib.ref_apply_rope.argtypes = [_P, _I, _I, _I, _P]
         lib.ref_apply_rope_rmsnorm.argtypes = [_P, _I, _I, _I, _P]
         lib.ref_flash_attention.argtypes = [_P, _P, _P, _P, _I, _I, _I, _F, _I, _P]
+        lib.ref_rmsnorm.argtypes = [_P, _P, _I, _I, _P]
+        lib.ref_embedding.argtypes = [_P, _P, _P, _I, _I, _P]
+        lib.ref_relu_squared.argtypes = [_P, _I, _P]
+        lib.ref_tanh_cap.argtypes = [_P, _I, _F, _P]
         for f in ("ref_init_rope_tables", "ref_get_rope_tables", "ref_apply_rope",
-                  "ref_apply_rope_rmsnorm", "ref_flash_attention"):
+                  "ref_apply_rope_rmsnorm", "ref_flash_attention", "ref_rmsnorm",
+                  "ref_embedding", "ref_relu_squared", "ref_tanh_cap"):
             getattr(lib, f).restype = _I
         _ref = lib
     return _ref

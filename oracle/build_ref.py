@@ -1,8 +1,8 @@
-"""TEST INFRASTRUCTURE ONLY: rebuild the reference's attention kernels for sm_100a.
+"""TEST INFRASTRUCTURE ONLY: rebuild the reference's kernels for sm_100a.
 
-Compiles kernels/rope.cu and kernels/flash_attention.cu of the reference project from where
-they lie (never copied) through oracle/ref_shim.cu, with the namespace renamed to
-nanochat_ref, into oracle/_ref/libref_attn.so.  The output is git-ignored but travels to the
+Compiles kernels/rope.cu, kernels/flash_attention.cu, kernels/rmsnorm.cu and kernels/ops.cu of
+the reference project from where they lie (never copied) through oracle/ref_shim.cu, with the
+namespace renamed to nanochat_ref, into oracle/_ref/libref_attn.so.  The output is git-ignored but travels to the
 GPU box with the working tree; the reference tree itself is only needed for this build.
 """
 import os
@@ -20,8 +20,9 @@ def build(ref_root=None, force=False, verbose=True):
     kdir = os.path.join(ref_root, "kernels")
     sdir = os.path.join(ref_root, "src")
     srcs = [os.path.join(kdir, "rope.cu"), os.path.join(kdir, "flash_attention.cu"),
+            os.path.join(kdir, "rmsnorm.cu"), os.path.join(kdir, "ops.cu"),
             os.path.join(HERE, "ref_shim.cu")]
-    if not all(os.path.exists(s) for s in srcs[:2]):
+    if not all(os.path.exists(s) for s in srcs[:4]):
         if verbose:
             print(f"[oracle] reference tree not found at {ref_root}; keeping existing {OUT}")
         return os.path.exists(OUT)

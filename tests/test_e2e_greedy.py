@@ -1,0 +1,224 @@
+"""End-to-end greedy decoding on the full 2.2B architecture (BASELINE cfg5 shapes), with the
+attention path on this library against the reference's own kernels.
+
+The engine below restates the reference's forward pass (src/model.cpp:101-167: embedding,
+RMSNorm, per layer RMSNorm -> Q/K/V projections -> RoPE + QK-norm -> KV append -> causal
+attention -> output projection + residual, RMSNorm -> MLP up -> ReLU^2 -> down + residual;
+final RMSNorm, LM head, tanh soft cap 15) and its greedy sampler (src/engine.cpp:88-95: first
+maximum; tokens 0 and 1 end generation, src/engine.cpp:55-56).  Both arms run the same
+non-attention work: the reference's own RMSNorm / embedding / ReLU^2 / tanh-cap kernels
+(kernels/rmsnorm.cu, kernels/ops.cu, rebuilt from source into oracle/_ref) and cuBLAS GEMMs
+with fp32 accumulation and a single rounding of product + residual (the reference's CUTLASS
+GEMM needs CUTLASS, which the reference does not vendor).  The arms differ only in the path
+this library replaces:
+
+* reference arm: two apply_rope_rmsnorm calls, two cache copies, flash_attention
+  (src/model.cpp:119-136) on the reference kernels;
+* library arm: nc_rope_qknorm_append (RoPE + QK-norm of q and k, k and v written into the
+  cache) and nc_flash_attention (tcgen05 prefill for the prompt, split-KV decode per token).
+
+A third arm computes attention exactly in fp32 with torch (reference RoPE/QK-norm kernels,
+then softmax(QK^T)V in fp32): it differs from the reference only in summation order and
+measures how far this random-weight network moves the logits under rounding alone.  Measured
+on B200, that floor is ~0.1 in max |logit difference| and 0.015 in mean, the same as the
+library arm; both arms flip greedy choices only where the reference's top-2 logits are 0-4
+bf16 ulps apart (ties included, which the reference breaks by index).  So free-running
+token identity over 32 steps holds only where no near-tie occurs, for any attention whose
+rounding differs from the reference's; the test therefore asserts the library against the
+fp32 floor and reports the free-running identity.
+
+Weights are random N(0, 0.02) in bf16 (seed 4), prompts are 256 token ids uniform in
+[0, 65536) (cfg5); 8 prompts, 32 greedy steps each.
+"""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+N_LAYER, N_HEAD, HEAD_DIM = 34, 17, 128
+N_EMBD = N_HEAD * HEAD_DIM          # 2176
+MLP_HIDDEN = 4 * N_EMBD              # 8704
+VOCAB = 65536
+LOGIT_CAP = 15.0
+MAX_LEN = 2048
+PROMPT_LEN = 256
+STEPS = 32
+N_PROMPTS = 8
+SCALE = 1.0 / math.sqrt(HEAD_DIM)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class Weights:
+    """Random-init weights in the reference's layout (src/model.h:30-47): W[out, in]."""
+
+    def __init__(self, seed=4, std=0.02):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g, device="cuda") * std).to(torch.bfloat16)
+
+        self.embed = rnd(VOCAB, N_EMBD)
+        self.layers = []
+        for _ in range(N_LAYER):
+            self.layers.append(dict(q=rnd(N_EMBD, N_EMBD), k=rnd(N_EMBD, N_EMBD),
+                                    v=rnd(N_EMBD, N_EMBD), o=rnd(N_EMBD, N_EMBD),
+                                    up=rnd(MLP_HIDDEN, N_EMBD), down=rnd(N_EMBD, MLP_HIDDEN)))
+        self.lm_head = rnd(VOCAB, N_EMBD)
+
+
+class Engine:
+    """One sequence at a time, as the reference's Engine (src/engine.cpp:37-62)."""
+
+    def __init__(self, w, ref, arm, nc=None):
+        self.w, self.ref, self.arm, self.nc = w, ref, arm, nc
+        self.stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self.kc = [torch.zeros(MAX_LEN, N_HEAD, HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+                   for _ in range(N_LAYER)]
+        self.vc = [torch.zeros_like(self.kc[0]) for _ in range(N_LAYER)]
+        self.pos = 0
+
+    def _rmsnorm(self, out, x, rows):
+        assert self.ref.ref_rmsnorm(_p(out), _p(x), rows, N_EMBD, self.stream) == 0
+
+    def _attention(self, layer, q, k, v, seq, start):
+        kv_len = start + seq
+        out = torch.empty(seq, N_EMBD, dtype=torch.bfloat16, device="cuda")
+        kc, vc = self.kc[layer], self.vc[layer]
+        if self.arm == "reference":
+            assert self.ref.ref_apply_rope_rmsnorm(_p(q), seq, N_HEAD, start, self.stream) == 0
+            assert self.ref.ref_apply_rope_rmsnorm(_p(k), seq, N_HEAD, start, self.stream) == 0
+            kc[start:kv_len].copy_(k.view(seq, N_HEAD, HEAD_DIM))
+            vc[start:kv_len].copy_(v.view(seq, N_HEAD, HEAD_DIM))
+            assert self.ref.ref_flash_attention(_p(out), _p(q), _p(kc), _p(vc), seq, kv_len,
+                                                N_HEAD, ctypes.c_float(SCALE), start,
+                                                self.stream) == 0
+        elif self.arm == "fp32":
+            assert self.ref.ref_apply_rope_rmsnorm(_p(q), seq, N_HEAD, start, self.stream) == 0
+            assert self.ref.ref_apply_rope_rmsnorm(_p(k), seq, N_HEAD, start, self.stream) == 0
+            kc[start:kv_len].copy_(k.view(seq, N_HEAD, HEAD_DIM))
+            vc[start:kv_len].copy_(v.view(seq, N_HEAD, HEAD_DIM))
+            qf = q.view(seq, N_HEAD, HEAD_DIM).float().transpose(0, 1)
+            sc = (qf @ kc[:kv_len].float().transpose(0, 1).transpose(1, 2)) * SCALE
+            qi = torch.arange(seq, device="cuda")[:, None] + start
+            kj = torch.arange(kv_len, device="cuda")[None, :]
+            sc = sc + torch.where(kj <= qi, 0.0, float("-inf"))
+            o = torch.softmax(sc, -1) @ vc[:kv_len].float().transpose(0, 1)
+            out.copy_(o.transpose(0, 1).reshape(seq, N_EMBD))
+        else:
+            self.nc.rope_qknorm_append(q, k, v, kc, vc, seq, N_HEAD, start)
+            self.nc.flash_attention(out, q, kc, vc, seq, kv_len, N_HEAD, SCALE, start)
+        return out
+
+    def forward(self, tokens):
+        """Logits (fp32 copy of the bf16 values) of the last position; advances the cache."""
+        seq, start = len(tokens), self.pos
+        tok = torch.tensor(tokens, dtype=torch.int32, device="cuda")
+        x = torch.empty(seq, N_EMBD, dtype=torch.bfloat16, device="cuda")
+        assert self.ref.ref_embedding(_p(x), _p(self.w.embed), _p(tok), seq, N_EMBD,
+                                      self.stream) == 0
+        self._rmsnorm(x, x, seq)
+        xn = torch.empty_like(x)
+        for i, l in enumerate(self.w.layers):
+            self._rmsnorm(xn, x, seq)
+            q = xn @ l["q"].t()
+            k = xn @ l["k"].t()
+            v = xn @ l["v"].t()
+            a = self._attention(i, q, k, v, seq, start)
+            x = torch.addmm(x, a, l["o"].t())
+            self._rmsnorm(xn, x, seq)
+            h = xn @ l["up"].t()
+            assert self.ref.ref_relu_squared(_p(h), h.numel(), self.stream) == 0
+            x = torch.addmm(x, h, l["down"].t())
+        self._rmsnorm(xn, x, seq)
+        logits = (xn[-1:] @ self.w.lm_head.t()).contiguous()
+        assert self.ref.ref_tanh_cap(_p(logits), VOCAB, ctypes.c_float(LOGIT_CAP), self.stream) == 0
+        self.pos += seq
+        return logits[0].float()
+
+    def generate(self, prompt, steps, forced=None):
+        """Greedy decode.  With `forced` (a token list), the next input is forced[t] instead
+        of this engine's own choice (teacher forcing); the choices are still returned."""
+        out, logits_all, inp = [], [], list(prompt)
+        for t in range(steps):
+            logits = self.forward(inp)
+            logits_all.append(logits)
+            c = int(torch.argmax(logits))  # first maximum, as the reference's strict '>' scan
+            out.append(c)
+            nxt = forced[t] if forced is not None else c
+            if nxt in (0, 1) or (forced is not None and t + 1 >= len(forced)):
+                break
+            inp = [nxt]
+        return out, torch.stack(logits_all)
+
+
+def bf16_ulp(x):
+    """Spacing of bf16 numbers at |x| (8 significant bits)."""
+    e = math.floor(math.log2(max(abs(x), 2.0 ** -126)))
+    return 2.0 ** (e - 7)
+
+
+@pytest.fixture(scope="module")
+def setup():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ref = oracle.reference_kernels()
+    if ref is None:
+        pytest.skip("reference kernels not built (oracle/_ref)")
+    import nanochat_inferonly_lightning_b200 as nc
+
+    assert ref.ref_init_rope_tables() == 0
+    nc.init_rope_tables()
+    w = Weights()
+    g = torch.Generator().manual_seed(4)
+    prompts = torch.randint(0, VOCAB, (N_PROMPTS, PROMPT_LEN), generator=g).tolist()
+    yield ref, nc, w, prompts
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) == 0, "a kernel's bounded wait gave up"
+
+
+def test_greedy_decode_against_reference(setup):
+    """Per prompt, the reference arm decodes 32 greedy tokens; the library and fp32 arms are
+    fed the same tokens (teacher forcing).  Asserted: (1) the library picks the reference's
+    token at every step except where the reference's logits of the two tokens are within
+    8 bf16 ulps (the measured rounding floor is ~6); (2) the library's logit deviation from the
+    reference is within 1.25x of the exact-fp32 arm's (mean) and within 0.25 (max).
+    Reported: exact matches, near-tie flips and free-running identity length per arm."""
+    ref, nc, w, prompts = setup
+    report, dev_lib, dev_f32, max_lib = [], [], [], 0.0
+    for n, prompt in enumerate(prompts):
+        want, lref = Engine(w, ref, "reference").generate(prompt, STEPS)
+        row = dict(prompt=n, steps=len(want))
+        for arm in ("library", "fp32"):
+            eng = lambda: Engine(w, ref, arm, nc)
+            forced, lx = eng().generate(prompt, len(want), forced=want)
+            free, _ = eng().generate(prompt, STEPS)
+            flips = []
+            for t, (a, b) in enumerate(zip(forced, want)):
+                if a != b:
+                    gap = (float(lref[t, b]) - float(lref[t, a])) / bf16_ulp(float(lref[t, b]))
+                    flips.append((t, round(gap, 1)))
+                    if arm == "library":
+                        assert gap <= 8.0, (
+                            f"prompt {n} step {t}: library picks {a}, reference {b}; reference "
+                            f"logits {gap:.1f} bf16 ulps apart")
+            d = (lx - lref[: len(lx)]).abs()
+            (dev_lib if arm == "library" else dev_f32).append(float(d.mean()))
+            if arm == "library":
+                max_lib = max(max_lib, float(d.max()))
+            first_free = next((i for i, (a, b) in enumerate(zip(free, want)) if a != b), len(want))
+            row[arm] = dict(flips=flips, free_run_identical=first_free,
+                            max_dlogit=round(float(d.max()), 3), mean_dlogit=round(float(d.mean()), 4))
+        report.append(row)
+    print("greedy decode vs reference:", report)
+    mean_lib, mean_f32 = sum(dev_lib) / len(dev_lib), sum(dev_f32) / len(dev_f32)
+    assert mean_lib <= 1.25 * mean_f32 + 1e-3, (mean_lib, mean_f32)
+    assert max_lib < 0.25, max_lib
