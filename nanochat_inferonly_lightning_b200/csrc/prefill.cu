@@ -357,75 +357,104 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                uint32_t sraw[128];
-                tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
-                float s[128];
-#pragma unroll
-                for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
                 const int key0 = j * kBN;
-                if (key0 + kBN - 1 > t.q0 + t.off || key0 + kBN > t.kv_len) {  // CTA-uniform
-                    const int lim = min(qlim + 1, t.kv_len) - key0;  // columns >= lim masked
-#pragma unroll
-                    for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
-                }
-                // Row max: 3-input max over pairs, eight independent chains.
-                float pm[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-                for (int c = 16; c < 128; c += 2)
-                    pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
-                const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
-                                       fmaxf(pm[6], pm[7]));
-                const float bm2 = bm * sl2;
-                const bool renew =
-                    (bm2 > m_ref + kRescaleThreshold) || (m_ref == kNegInf && bm2 != kNegInf);
-                float alpha = 1.f;
-                if (renew) {
-                    alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
-                    m_ref = bm2;
-                }
-                l *= alpha;
-                // Rescale O for rows that renewed; O must first hold PV(g-1) complete.
-                if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
-                    const int sp = (g - 1) & 1;
-                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarPV + sp], ((g - 1) >> 1) & 1,
-                                                           abort_flag, p.status, 11))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t raw[32];
-                        tmem_ld32_sync(tO + 32 * c, raw);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
-                        tmem_st32_sync(tO + 32 * c, raw);
-                    }
-                }
-                const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
-                // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and the
-                // row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
-                // polynomial instead of MUFU.  Masked scores are -inf and give exactly 0.
+                // Two ways through a block.  Exact: row max first, then the reference max is
+                // renewed (O and the row sum rescaled) if the block max exceeds it by more than
+                // the threshold, then P.  Optimistic: once every row of the warp has a finite
+                // reference, P is computed against it straight away; the block needed no renewal
+                // exactly when no P exceeds 2^threshold, which the block's row sum bounds (each
+                // P <= the sum), so a sum <= 2^threshold accepts the block and anything else
+                // (or NaN) redoes it the exact way.  After a tile's first block the optimistic
+                // path almost always holds and the max pass is skipped.
                 const uint64_t sl2x2 = f2_pack(sl2, sl2);
-                const uint64_t nmu2 = f2_pack(-mu, -mu);
-                uint64_t acc2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+                uint64_t acc2[2];
                 uint32_t pk[64];
+                bool exact = __any_sync(0xFFFFFFFFu, m_ref == kNegInf);
+                for (;;) {
+                    // S is (re)loaded from TMEM on each way through: it stays there until QK(g+2),
+                    // which waits for P(g), and reloading is cheaper than keeping 128 scores
+                    // live across a possible second pass.
+                    uint32_t sraw[128];
+                    tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
+                    float s[128];
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    float x0, x1, p0, p1;
-                    f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
-                    if ((i & 3) == 3) {
-                        exp2_poly2(x0, x1, p0, p1);
-                    } else {
-                        p0 = fast_exp2(x0);
-                        p1 = fast_exp2(x1);
+                    for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
+                    if (key0 + kBN - 1 > t.q0 + t.off || key0 + kBN > t.kv_len) {  // CTA-uniform
+                        const int lim = min(qlim + 1, t.kv_len) - key0;  // columns >= lim masked
+#pragma unroll
+                        for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
                     }
-                    acc2[i & 1] = f2_add(acc2[i & 1], f2_pack(p0, p1));
-                    pk[i] = pack_bf16x2(p0, p1);
+                    if (exact) {
+                        // Row max: 3-input max over pairs, eight independent chains.
+                        float pm[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+                        for (int c = 16; c < 128; c += 2)
+                            pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
+                        const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                                               fmaxf(pm[6], pm[7]));
+                        const float bm2 = bm * sl2;
+                        const bool renew = (bm2 > m_ref + kRescaleThreshold) ||
+                                           (m_ref == kNegInf && bm2 != kNegInf);
+                        float alpha = 1.f;
+                        if (renew) {
+                            alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
+                            m_ref = bm2;
+                        }
+                        l *= alpha;
+                        // Rescale O for rows that renewed; O must first hold PV(g-1) complete.
+                        if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
+                            const int sp = (g - 1) & 1;
+                            if (!__all_sync(0xFFFFFFFFu,
+                                            mbar_wait(&bars[kBarPV + sp], ((g - 1) >> 1) & 1,
+                                                      abort_flag, p.status, 11))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                uint32_t raw[32];
+                                tmem_ld32_sync(tO + 32 * c, raw);
+#pragma unroll
+                                for (int i = 0; i < 32; ++i)
+                                    raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
+                                tmem_st32_sync(tO + 32 * c, raw);
+                            }
+                        }
+                    }
+                    const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
+                    // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and
+                    // the row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
+                    // polynomial (input clamped to 127 so that it stays monotone) instead of
+                    // MUFU.  Masked scores are -inf and give exactly 0.
+                    const uint64_t nmu2 = f2_pack(-mu, -mu);
+                    acc2[0] = f2_pack(0.f, 0.f);
+                    acc2[1] = f2_pack(0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        float x0, x1, p0, p1;
+                        f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
+                        if ((i & 3) == 3) {
+                            exp2_poly2(fminf(x0, 127.f), fminf(x1, 127.f), p0, p1);
+                        } else {
+                            p0 = fast_exp2(x0);
+                            p1 = fast_exp2(x1);
+                        }
+                        acc2[i & 1] = f2_add(acc2[i & 1], f2_pack(p0, p1));
+                        pk[i] = pack_bf16x2(p0, p1);
+                    }
+                    if (exact) break;
+                    float c0, c1, d0, d1;
+                    f2_unpack(acc2[0], c0, c1);
+                    f2_unpack(acc2[1], d0, d1);
+                    const float bsum = (c0 + c1) + (d0 + d1);
+                    constexpr float kRenewSum = 256.0f;  // 2^kRescaleThreshold
+                    exact = __any_sync(0xFFFFFFFFu, !(bsum <= kRenewSum));
+                    if (!exact) break;
                 }
+                if (!ok) break;
                 float a0, a1, b0, b1;
                 f2_unpack(acc2[0], a0, a1);
                 f2_unpack(acc2[1], b0, b1);
