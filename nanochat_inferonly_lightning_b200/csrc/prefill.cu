@@ -192,6 +192,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    // The kernel is launched with programmatic stream serialization: everything above (barrier
+    // init, TMEM allocation, tensor-map prefetch) may overlap the tail of the previous kernel
+    // in the stream, typically the RoPE/append pass that writes Q, K and V.  No global memory
+    // is read or written before this wait, which returns once that kernel has completed and
+    // its writes are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // Ring positions are driven by g, the running count of key blocks this CTA has visited
     // (stage g & 1, parity (g >> 1) & 1), and by qi, the running count of non-empty tiles
@@ -643,8 +649,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     kp.status = a.status;
     // Persistent: one CTA per SM (or fewer when there are fewer tiles).
     const unsigned grid = (unsigned)std::min<long long>(kp.total_tiles, sm_count[dev]);
-    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, kp);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_kernel, mq, mk, mv, kp);
 }
 
 }  // namespace nc

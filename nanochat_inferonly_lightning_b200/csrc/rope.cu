@@ -104,6 +104,10 @@ __device__ __forceinline__ void rope_norm_pairs(const float4 (&cs)[4], uint4 lo,
 // the attention kernel that reads them next.
 template <int MODE>
 __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
+    // Lets a kernel launched after this one with programmatic stream serialization (the
+    // prefill attention kernel) start its setup early; it still waits for this grid to
+    // complete before it reads any of this pass's outputs.
+    asm volatile("griddepcontrol.launch_dependents;");
     const int grp = (blockIdx.x * kRopeThreads + threadIdx.x) >> 3;
     const int stride = (gridDim.x * kRopeThreads) >> 3;
     const int s8 = threadIdx.x & 7;
