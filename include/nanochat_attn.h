@@ -93,9 +93,11 @@ size_t nc_decode_workspace_bytes(int batch, int max_kv_len, int heads, int split
  *           kv_len[b]-1), 1 <= kv_len[b] <= max_kv_len.
  *   split_len  keys per split-KV chunk (multiple of 16) or 0 for automatic.
  *   workspace  >= nc_decode_workspace_bytes(...) bytes, zero-filled before first use and
- *           again before a call with a larger batch than any earlier call on it; its first
- *           4*batch bytes are split counters that each call leaves at zero.  Calls sharing
- *           one workspace must not overlap on the GPU.
+ *           again before a call with a larger batch than any earlier call on it; it starts
+ *           with (2 + batch*heads) 32-bit counters (a work queue, an exit count and one split
+ *           ticket per sequence and head) that each call leaves at zero, so a call can be
+ *           captured in a CUDA graph and replayed.  Calls sharing one workspace must not
+ *           overlap on the GPU.
  * Replaces: the seq_len == 1 path of Model::attention (src/model.cpp:119-136): two
  * apply_rope_rmsnorm launches, two append copies and flash_attention, for one sequence. */
 int nc_decode_attention(void* out, const void* q, const void* k_new, const void* v_new,

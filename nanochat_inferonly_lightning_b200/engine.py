@@ -1,0 +1,155 @@
+"""Batched greedy generation on the reference model's architecture, with its attention path on
+this library.
+
+The forward pass follows the reference's Model (src/model.cpp:101-167): embedding, RMSNorm;
+per layer RMSNorm -> Q/K/V projections -> RoPE + QK-norm -> KV append -> causal attention ->
+output projection + residual, then RMSNorm -> MLP up -> ReLU^2 -> down + residual; final RMSNorm,
+LM head, tanh soft cap 15.  Sampling is the reference's greedy rule (src/engine.cpp:88-95,
+first maximum).  Weights use the reference's layout W[out, in] (src/model.h:30-47).
+
+What runs where:
+* the attention path (the part this library replaces) on this library: for a prompt,
+  nc_rope_qknorm_append + nc_flash_attention per sequence (tcgen05 prefill); for each decode
+  step, one nc_decode_attention over the whole batch (RoPE + QK-norm of q and k, append, and
+  split-KV attention in one kernel), reading per-sequence lengths from a device array;
+* GEMMs on cuBLAS through torch (fp32 accumulation; product + residual rounded once), and the
+  parameter-free RMSNorm, ReLU^2, tanh cap and embedding gather as torch operations.
+
+A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
+and replayed; the device length array advances inside the graph.  The reference engine runs one
+sequence at a time with host-side lengths (src/engine.cpp:37-62); here a batch of sequences
+advances together.
+"""
+import math
+
+import torch
+
+from . import attn
+
+N_LAYER = 34
+N_HEAD = 17
+HEAD_DIM = 128
+N_EMBD = N_HEAD * HEAD_DIM   # 2176
+MLP_HIDDEN = 4 * N_EMBD      # 8704
+VOCAB = 65536
+LOGIT_CAP = 15.0
+NORM_EPS = 1e-6
+SCALE = 1.0 / math.sqrt(HEAD_DIM)
+
+
+class Weights:
+    """Random-init weights N(0, std) in bf16 on the current device (the architecture of
+    src/config.h: 34 layers, d_model 2176, 17 heads x 128, MLP 8704, vocab 65536)."""
+
+    def __init__(self, seed=4, std=0.02, device="cuda"):
+        g = torch.Generator(device=device).manual_seed(seed)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+        self.embed = rnd(VOCAB, N_EMBD)
+        self.layers = []
+        for _ in range(N_LAYER):
+            self.layers.append(dict(q=rnd(N_EMBD, N_EMBD), k=rnd(N_EMBD, N_EMBD),
+                                    v=rnd(N_EMBD, N_EMBD), o=rnd(N_EMBD, N_EMBD),
+                                    up=rnd(MLP_HIDDEN, N_EMBD), down=rnd(N_EMBD, MLP_HIDDEN)))
+        self.lm_head = rnd(VOCAB, N_EMBD)
+
+
+def rmsnorm(x):
+    """Parameter-free RMSNorm in fp32 (kernels/rmsnorm.cu: x * rsqrt(mean(x^2) + 1e-6))."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + NORM_EPS)).to(torch.bfloat16)
+
+
+def logits_of(w, x):
+    """Final RMSNorm, LM head, tanh soft cap (src/model.cpp:147-155)."""
+    lg = (rmsnorm(x) @ w.lm_head.t()).float()
+    return (LOGIT_CAP * torch.tanh(lg / LOGIT_CAP)).to(torch.bfloat16)
+
+
+class BatchedEngine:
+    """`batch` sequences, each with KV caches of `max_len` rows per layer."""
+
+    def __init__(self, weights, batch, max_len, device="cuda"):
+        self.w, self.B, self.max_len = weights, batch, max_len
+        attn.init_rope_tables()
+        shape = (batch, max_len, N_HEAD, HEAD_DIM)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        row = max_len * N_HEAD * HEAD_DIM * 2
+
+        def table(t):
+            return torch.tensor([t.data_ptr() + b * row for b in range(batch)], dtype=torch.int64,
+                                device=device)
+
+        self.k_tab = [table(t) for t in self.k]
+        self.v_tab = [table(t) for t in self.v]
+        self.kv_len = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.ws = torch.zeros(attn.decode_workspace_bytes(batch, max_len, N_HEAD),
+                              dtype=torch.uint8, device=device)
+        self.tok = torch.zeros(batch, dtype=torch.int64, device=device)  # next input token
+        self.logits = None
+        self.graph = None
+
+    # ------------------------------------------------------------------ prompt
+    def prefill(self, prompts):
+        """prompts: int64 [B, P] token ids; fills the caches and sets the first generated
+        token of every sequence (returned, and kept as the next decode input)."""
+        B, P = prompts.shape
+        assert B == self.B and P < self.max_len
+        w = self.w
+        first = torch.empty(B, dtype=torch.int64, device=prompts.device)
+        for b in range(B):
+            x = rmsnorm(w.embed[prompts[b]])
+            for i, l in enumerate(w.layers):
+                xn = rmsnorm(x)
+                q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
+                a = torch.empty_like(q)
+                attn.rope_qknorm_append(q, k, v, self.k[i][b], self.v[i][b], P, N_HEAD, 0)
+                attn.flash_attention(a, q, self.k[i][b], self.v[i][b], P, P, N_HEAD, SCALE, 0)
+                x = torch.addmm(x, a, l["o"].t())
+                h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
+                x = torch.addmm(x, h, l["down"].t())
+            first[b] = torch.argmax(logits_of(w, x[-1:])[0].float())
+        self.kv_len.fill_(P)
+        self.tok.copy_(first)
+        return first
+
+    # ------------------------------------------------------------------ decode
+    def _decode_body(self):
+        """One greedy step for the whole batch: consumes self.tok, writes the next tokens back
+        into self.tok.  Static shapes, device-side lengths: safe to capture."""
+        w = self.w
+        self.kv_len.add_(1)  # the new token sits at row kv_len - 1
+        x = rmsnorm(w.embed[self.tok])
+        for i, l in enumerate(w.layers):
+            xn = rmsnorm(x)
+            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
+            a = torch.empty_like(q)
+            attn.decode_attention(a, q, k, v, self.k_tab[i], self.v_tab[i], self.kv_len, N_HEAD,
+                                  SCALE, self.max_len, self.ws)
+            x = torch.addmm(x, a, l["o"].t())
+            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
+            x = torch.addmm(x, h, l["down"].t())
+        self.logits = logits_of(w, x)  # [B, VOCAB] bf16, kept for inspection
+        self.tok.copy_(torch.argmax(self.logits.float(), dim=-1))
+
+    def capture(self):
+        """Capture one decode step in a CUDA graph (after one eager warm-up step, which also
+        performs every per-device set-up outside the capture).  The warm-up step advances
+        the sequences like any other step."""
+        self._decode_body()
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._decode_body()
+        return self.tok.clone()
+
+    def step(self):
+        """One decode step (graph replay if captured); returns the new tokens (device)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._decode_body()
+        return self.tok
