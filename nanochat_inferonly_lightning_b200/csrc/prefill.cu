@@ -14,8 +14,8 @@
 // overlap the current tile's last blocks and epilogue.
 //
 // Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producers: lane 0 each tile's Q (two buffers) and K(j) into a two-stage
-//               ring, lane 1 V(j) into a two-stage ring.
+//   warp 0      TMA producers: lane 0 K(j) into a two-stage ring, lane 1 V(j) into a
+//               two-stage ring, lane 2 each tile's Q (two buffers).
 //   warp 1      allocates all 512 TMEM columns; one lane issues every tcgen05.mma.
 //   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
 // Tensor memory (512 columns): S0 [0,128) and S1 [128,256) hold Q.K^T of consecutive key
@@ -204,10 +204,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (Q buffer qi & 1, parity (qi >> 1) & 1).
     if (warp == 0) {
         // ------------------------------------------------------------------ producers
-        // Lane 0 loads Q and K, lane 1 loads V, each waiting only on the barrier that frees
-        // its own ring, so K(g+2) streams in as soon as QK(g) is done, independently of V.
-        if (lane < 2) {
+        // Lane 0 loads K, lane 1 loads V and lane 2 loads Q, each waiting only on the barrier
+        // that frees its own ring: K(g+2) streams in as soon as QK(g) is done, V(g+2) once
+        // PV(g) is, and a tile's Q as soon as its buffer's previous tile has finished its QKs
+        // (up to two tiles ahead), so the next tile's first QK never waits behind K loads.
+        if (lane < 3) {
             const bool kq = lane == 0;
+            const bool qload = lane == 2;
             int g = 0, qi = 0;
             bool ok = true;
             for (int k = 0; ok; ++k) {
@@ -216,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const Tile t = make_tile(p, rank);
                 if (t.nb == 0) continue;
                 const int x0 = t.h * 128;
-                if (kq) {
+                if (qload) {
                     const int qb = qi & 1;
                     if (qi >= 2 && !(ok = mbar_wait(&bars[kBarQFree + qb], ((qi >> 1) - 1) & 1,
                                                     abort_flag, p.status, 1)))
@@ -225,6 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&bars[kBarQ + qb], kTileBytes);
                     tma_load_3d(dq, &tmQ, &bars[kBarQ + qb], x0, t.q0, t.b);
                     tma_load_3d(dq + kBoxBytes, &tmQ, &bars[kBarQ + qb], x0 + 64, t.q0, t.b);
+                    ++qi;
+                    continue;
                 }
                 for (int j = 0; j < t.nb; ++j, ++g) {
                     const int st = g & 1;
@@ -243,9 +248,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++qi;
             }
             // Do not leave with loads still landing in shared memory: the last loads of each
-            // ring are consumed by MMAs whose completion arrives on kBarS (K) / kBarPV (V).
-            for (int x = max(g - 2, 0); x < g; ++x)
-                mbar_wait(&bars[(kq ? kBarS : kBarPV) + (x & 1)], (x >> 1) & 1, abort_flag, p.status, 3);
+            // ring are consumed by MMAs whose completion arrives on kBarS (K) / kBarPV (V); every
+            // Q load is waited for by the MMA warp before that tile's first QK.
+            if (!qload)
+                for (int x = max(g - 2, 0); x < g; ++x)
+                    mbar_wait(&bars[(kq ? kBarS : kBarPV) + (x & 1)], (x >> 1) & 1, abort_flag,
+                              p.status, 3);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -323,6 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_ts_warp(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
                                 kk > 0 ? 1u : acc0);
                 }
+                // The tile's output is complete once its last P.V is: the epilogue does not
+                // wait behind the next tile's QK.
+                if (j + 1 == nb) mma_commit_warp(&bars[kBarOFinal]);
                 // softmax(g) has read S(g & 1) (it wrote P(g) afterwards), so QK(g+2) may
                 // refill it.
                 if (ahead.valid) {
@@ -335,7 +346,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // stretch (measured: committing right after the P.V MMAs made the next QK
                 // batch ~4x slower).
                 mma_commit_warp(&bars[kBarPV + st]);
-                if (j + 1 == nb) mma_commit_warp(&bars[kBarOFinal]);
             }
         }
     } else {
