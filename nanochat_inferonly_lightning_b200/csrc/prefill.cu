@@ -71,8 +71,9 @@ struct __align__(8) SmemTail {
     int abort;
 };
 
-// Two Q buffers + two K stages + two V stages.
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 6 * kTileBytes + sizeof(SmemTail);
+// Two Q buffers + two K stages + two V stages + the output staging tile.
+constexpr uint32_t kStageOutBytes = 128 * 128 * 2;  // 4 warps x (32 rows x 256 B)
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + 6 * kTileBytes + kStageOutBytes + sizeof(SmemTail);
 
 struct PrefillKParams {
     bf16* out;
@@ -157,16 +158,32 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* t
         : "memory");
 }
 
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tmap, const void* smem_src, int x,
+                                             int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tmap)),
+        "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const PrefillKParams p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                   const PrefillKParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sQ = smem;                    // buffers at sQ, sQ + kTileBytes
     uint8_t* sK = smem + 2 * kTileBytes;   // stages at sK, sK + kTileBytes
     uint8_t* sV = smem + 4 * kTileBytes;   // stages at sV, sV + kTileBytes
-    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 6 * kTileBytes);
+    uint8_t* sO = smem + 6 * kTileBytes;   // output staging, 8 KB per softmax warp
+    SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 6 * kTileBytes + kStageOutBytes);
     uint64_t* bars = tail->bars;
     volatile int* abort_flag = &tail->abort;
 
@@ -187,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmQ);
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
+        prefetch_tmap(&tmO);
     }
     tc_fence_before();
     __syncthreads();
@@ -503,29 +521,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++qi;
             tc_fence_after();
             const float inv = 1.0f / l;  // l == 0 (no visible key) gives 0 * inf = NaN
+            // The warp stages its 32 rows in shared memory in the 128B-swizzled layout of a
+            // (64 dims x 32 rows) box, two boxes per row, and lane 0 writes them with two TMA
+            // stores: whole lines reach L2 instead of 32 scattered 16-byte pieces per store
+            // instruction.  The staging area is reused only after the previous stores from it
+            // have finished reading it.  Rows at or past seq_q are clipped by the tensor map.
+            uint8_t* stg = sO + quarter * 8192;
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t raw[32];
                 tmem_ld32_sync(tO + 32 * c, raw);
-                if (store) {
-                    uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint4 w;
-                        w.x = pack_bf16x2(__uint_as_float(raw[8 * i + 0]) * inv,
-                                          __uint_as_float(raw[8 * i + 1]) * inv);
-                        w.y = pack_bf16x2(__uint_as_float(raw[8 * i + 2]) * inv,
-                                          __uint_as_float(raw[8 * i + 3]) * inv);
-                        w.z = pack_bf16x2(__uint_as_float(raw[8 * i + 4]) * inv,
-                                          __uint_as_float(raw[8 * i + 5]) * inv);
-                        w.w = pack_bf16x2(__uint_as_float(raw[8 * i + 6]) * inv,
-                                          __uint_as_float(raw[8 * i + 7]) * inv);
-                        dst[i] = w;
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    uint4 w;
+                    w.x = pack_bf16x2(__uint_as_float(raw[8 * i + 0]) * inv,
+                                      __uint_as_float(raw[8 * i + 1]) * inv);
+                    w.y = pack_bf16x2(__uint_as_float(raw[8 * i + 2]) * inv,
+                                      __uint_as_float(raw[8 * i + 3]) * inv);
+                    w.z = pack_bf16x2(__uint_as_float(raw[8 * i + 4]) * inv,
+                                      __uint_as_float(raw[8 * i + 5]) * inv);
+                    w.w = pack_bf16x2(__uint_as_float(raw[8 * i + 6]) * inv,
+                                      __uint_as_float(raw[8 * i + 7]) * inv);
+                    const int d = 32 * c + 8 * i;              // first of the 8 dims in w
+                    const int granule = ((d & 63) >> 3) ^ (lane & 7);  // 16-byte unit, swizzled
+                    *reinterpret_cast<uint4*>(stg + (d >> 6) * 4096 + lane * 128 + granule * 16) = w;
                 }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            const int y0 = t.q0 + quarter * 32;
+            if (lane == 0 && y0 < p.seq_q) {
+                tma_store_3d(&tmO, stg, t.h * 128, y0, t.b);
+                tma_store_3d(&tmO, stg + 4096, t.h * 128 + 64, y0, t.b);
+                bulk_commit();
             }
             tc_fence_before();
         }
+        // Output stores still reading the staging tile must finish before the CTA exits.
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -557,16 +593,17 @@ EncodeTiledFn get_encode_fn() {
     return fn;
 }
 
-// 3-D map over [batch][rows][heads*128] bf16 with a (64 dims, 128 rows, 1) box, 128B swizzle.
+// 3-D map over [batch][rows][heads*128] bf16 with a (64 dims, box_rows rows, 1) box, 128B
+// swizzle.
 bool make_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
-              long long batch_stride_elems) {
+              long long batch_stride_elems, int box_rows) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)heads * 128, (cuuint64_t)rows, (cuuint64_t)batch};
     const cuuint64_t strides[2] = {(cuuint64_t)heads * 128 * 2,
                                    (cuuint64_t)(batch > 1 ? batch_stride_elems * 2
                                                           : (long long)rows * heads * 128 * 2)};
-    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -579,11 +616,11 @@ bool make_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
 // encoding work.  Small direct-mapped table; a collision just re-encodes.
 struct MapKey {
     const void* base;
-    int heads, rows, batch, dev;
+    int heads, rows, batch, dev, box_rows;
     long long stride;
     bool operator==(const MapKey& o) const {
         return base == o.base && heads == o.heads && rows == o.rows && batch == o.batch &&
-               dev == o.dev && stride == o.stride;
+               dev == o.dev && box_rows == o.box_rows && stride == o.stride;
     }
 };
 struct MapEntry {
@@ -595,11 +632,11 @@ std::mutex g_map_mutex;
 MapEntry g_maps[256];
 
 bool cached_map(CUtensorMap* m, const void* base, int heads, int rows, int batch,
-                long long batch_stride_elems, int dev) {
-    const MapKey key{base, heads, rows, batch, dev, batch_stride_elems};
+                long long batch_stride_elems, int dev, int box_rows) {
+    const MapKey key{base, heads, rows, batch, dev, box_rows, batch_stride_elems};
     size_t h = reinterpret_cast<uintptr_t>(base) >> 8;
     h ^= (size_t)rows * 0x9E3779B1u ^ (size_t)heads * 0x85EBCA6Bu ^ (size_t)batch * 0xC2B2AE35u ^
-         (size_t)dev * 0x27D4EB2Fu ^ (size_t)batch_stride_elems;
+         (size_t)dev * 0x27D4EB2Fu ^ (size_t)batch_stride_elems ^ (size_t)box_rows * 0x165667B1u;
     MapEntry& e = g_maps[h & 255];
     {
         std::lock_guard<std::mutex> lk(g_map_mutex);
@@ -608,7 +645,7 @@ bool cached_map(CUtensorMap* m, const void* base, int heads, int rows, int batch
             return true;
         }
     }
-    if (!make_map(m, base, heads, rows, batch, batch_stride_elems)) return false;
+    if (!make_map(m, base, heads, rows, batch, batch_stride_elems, box_rows)) return false;
     std::lock_guard<std::mutex> lk(g_map_mutex);
     e.key = key;
     e.map = *m;
@@ -633,11 +670,15 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     const int kv_rows = a.kv_rows;
-    if (!cached_map(&mq, a.q, a.heads, a.seq_q, a.batch, (long long)a.seq_q * a.heads * 128, dev) ||
-        !cached_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev) ||
-        !cached_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev))
+    const long long qo_stride = (long long)a.seq_q * a.heads * 128;
+    // Q/K/V loads move (64 dims x 128 rows) boxes; the output is stored by each softmax warp
+    // in (64 dims x 32 rows) boxes.
+    if (!cached_map(&mq, a.q, a.heads, a.seq_q, a.batch, qo_stride, dev, 128) ||
+        !cached_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev, 128) ||
+        !cached_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev, 128) ||
+        !cached_map(&mo, a.out, a.heads, a.seq_q, a.batch, qo_stride, dev, 32))
         return cudaErrorInvalidValue;
     PrefillKParams kp;
     kp.out = a.out;
@@ -669,7 +710,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_kernel, mq, mk, mv, kp);
+    return cudaLaunchKernelEx(&cfg, prefill_kernel, mq, mk, mv, mo, kp);
 }
 
 }  // namespace nc
