@@ -62,6 +62,7 @@ enum Bar : int {
     kBarP = kBarS + 2,           // [2] softmax wrote P(g)
     kBarPV = kBarP + 2,          // [2] PV(g) done: V stage free, P(g & 1) free
     kBarOFinal = kBarPV + 2,
+    kBarDrain = kBarOFinal + 1,  // the MMA warp's last commit: every MMA it issued is done
     kNumBars
 };
 
@@ -265,13 +266,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++qi;
             }
-            // Do not leave with loads still landing in shared memory: the last loads of each
-            // ring are consumed by MMAs whose completion arrives on kBarS (K) / kBarPV (V); every
-            // Q load is waited for by the MMA warp before that tile's first QK.
+            // Do not leave with loads still landing in shared memory.  On the normal path the
+            // last loads of each ring are consumed by MMAs whose completion arrives on kBarS (K)
+            // / kBarPV (V), and every Q load is waited for before that tile's first QK.  After
+            // an abort, the last load issued into each stage or buffer must still land: its
+            // full barrier completes then (on the normal path these waits return at once).
             if (!qload)
                 for (int x = max(g - 2, 0); x < g; ++x)
                     mbar_wait(&bars[(kq ? kBarS : kBarPV) + (x & 1)], (x >> 1) & 1, abort_flag,
                               p.status, 3);
+            const int issued = qload ? qi : g;
+            const int full = qload ? kBarQ : (kq ? kBarKFull : kBarVFull);
+            for (int x = max(issued - 2, 0); x < issued; ++x)
+                mbar_wait_drain(&bars[full + (x & 1)], (x >> 1) & 1, p.status, 12);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -366,6 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_commit_warp(&bars[kBarPV + st]);
             }
         }
+        // Leave only once every MMA issued above has completed, aborted or not: TMEM is
+        // released after the block barrier below, and no MMA may still read shared memory or
+        // write TMEM then.
+        mma_commit_warp(&bars[kBarDrain]);
+        mbar_wait_drain(&bars[kBarDrain], 0, p.status, 13);
     } else {
         // ------------------------------------------------------------------ softmax / epilogue
         const int quarter = warp & 3;

@@ -14,10 +14,13 @@ namespace nc {
 // __device__ int whose address the host passes in); the host reads and clears it through
 // nc_device_status().
 constexpr int kStatusTimeoutMbar = 0x100;   // an mbarrier wait ran past its limit
+constexpr int kStatusBounds = 0x400;        // a kernel's own index check failed (access skipped)
 
 // Wall-clock limit for any single wait inside a kernel (nanoseconds).  A correct kernel
 // waits microseconds; one second means something upstream is broken.
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+// Limit for the waits a block takes while it leaves (its own copies and MMAs in flight).
+constexpr unsigned long long kDrainLimitNs = 100000000ull;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -84,6 +87,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                 atomicOr(status, kStatusTimeoutMbar | tag);
                 return false;
             }
+        }
+    }
+}
+
+// Wait taken while a block leaves, on the completion of copies or MMAs it issued itself:
+// bounded by time but not cut short by the abort flag, so that nothing still writes shared
+// memory or TMEM once they are released.  Records kStatusTimeoutMbar | tag if it gives up.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* status,
+                                                int tag) {
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > kDrainLimitNs) {
+            atomicOr(status, kStatusTimeoutMbar | tag);
+            return false;
         }
     }
 }
