@@ -83,6 +83,9 @@ int auto_split_len(int batch, int max_kv_len) {
     const long long est_keys = batch > 1 ? (long long)batch * max_kv_len / 2 : max_kv_len;
     const long long target = 148LL * 4;
     long long t = (est_keys + target - 1) / target;
+    // At most 32 splits per sequence: the last split of a head combines all of them, and
+    // beyond that the combine's round trips outweigh the extra parallelism.
+    t = std::max<long long>(t, (max_kv_len + 31) / 32);
     t = (t + 15) / 16 * 16;
     return (int)std::min<long long>(std::max<long long>(t, 16), 1024);
 }

@@ -7,8 +7,9 @@
 // src/model.cpp:119-131.
 //
 // Work items are (sequence, split): `split_len` consecutive keys of one sequence, all heads.
-// The kernel is persistent (one CTA per SM).  Lane 0 of the last warp is the producer: it
-// pulls items from a global atomic counter and streams each item's K and V rows (a cache row
+// The kernel is persistent (at most one CTA per SM, never more CTAs than items).  Lane 0 of
+// the last warp is the producer: its first item is its CTA index, further items (when there
+// are more items than CTAs) come from a global atomic counter; it streams each item's K and V rows (a cache row
 // holds every head, heads*256 contiguous bytes, so R rows are one contiguous block) into a
 // three-stage shared-memory ring with bulk asynchronous copies (cp.async.bulk, completion on
 // an mbarrier).  The bytes in flight per SM are therefore set by the ring (three stages of
@@ -112,8 +113,17 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 return use == 0 ||
                        mbar_wait(&tail->empty[s], (use - 1) & 1, abort_flag, a.status, 0x21);
             };
-            for (;;) {
-                const int i = (int)atomicAdd(a.counters, 1u);
+            // The first item is the CTA's own index; only when there are more items than CTAs
+            // do CTAs take further items from the queue (and then all of them reset it below).
+            const bool queue = total_items > (int)gridDim.x;
+            for (int first_item = 1;; first_item = 0) {
+                int i;
+                if (first_item) {
+                    i = (int)blockIdx.x;
+                } else {
+                    if (!queue) break;
+                    i = (int)gridDim.x + (int)atomicAdd(a.counters, 1u);
+                }
                 if (i >= total_items) break;
                 const int split = i / a.batch;
                 const int b = i - split * a.batch;
@@ -162,10 +172,12 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 ++n;
             }
             // Leave the queue ready for the next launch once every CTA has stopped fetching.
-            __threadfence();
-            if (atomicAdd(a.counters + 1, 1u) == gridDim.x - 1) {
-                a.counters[0] = 0u;
-                a.counters[1] = 0u;
+            if (queue) {
+                __threadfence();
+                if (atomicAdd(a.counters + 1, 1u) == gridDim.x - 1) {
+                    a.counters[0] = 0u;
+                    a.counters[1] = 0u;
+                }
             }
             // Do not leave with copies still landing: the data stages armed last are
             // released by the consumers before they exit (the terminator is not released).
@@ -186,6 +198,32 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
         float qf[8], acc[8], m = kNegInf, l = 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) qf[e] = acc[e] = 0.f;
+        // The query of sequence qf_b, scaled and (fused form) after RoPE + QK-norm.  It only
+        // depends on the sequence, so it is kept across that sequence's items, and the CTA's
+        // first item (its own index) is known up front: that query is prepared while the
+        // producer's first copies are in flight.
+        int qf_b = -1;
+        auto load_query = [&](int b, int L) {
+            const size_t qoff = (size_t)b * rowstride + (size_t)h * kHeadDim + 8 * sub;
+            const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
+            if (a.q_raw) {
+                float y[8];
+                rope_norm_row(a.rope_cs, qr, sub, hmask, max(L - 1, 0), true, y);
+                bf16x8_to_f32(f32_to_bf16x8(y), qf);  // bf16 like the unfused path
+            } else {
+                bf16x8_to_f32(qr, qf);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qf[e] *= a.scale_log2;
+            qf_b = b;
+        };
+        if ((int)blockIdx.x < total_items) {
+            const int b0 = (int)blockIdx.x % a.batch;
+            load_query(b0, min(raw_len(a, b0), a.max_kv_len));
+        }
+        // The new token's key (after RoPE + QK-norm) and value, prepared at the start of the
+        // item that ends at it, and used after the item's cached rows.
+        uint4 new_k = make_uint4(0u, 0u, 0u, 0u), new_v = new_k;
         unsigned n = 0;
         for (;;) {
             const int s = (int)(n % kStages);
@@ -201,55 +239,67 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 l = 0.f;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-                const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
-                if (a.q_raw) {
+                if (b != qf_b) load_query(b, hd.L);
+                const int ke0 = min(hd.L, hd.split * a.split_len + a.split_len);
+                if (a.k_new != nullptr && hd.L > 0 && ke0 == hd.L) {
+                    const uint4 kr = *reinterpret_cast<const uint4*>(a.k_new + qoff);
+                    new_v = *reinterpret_cast<const uint4*>(a.v_new + qoff);
                     float y[8];
-                    rope_norm_row(a.rope_cs, qr, sub, hmask, max(hd.L - 1, 0), true, y);
-                    bf16x8_to_f32(f32_to_bf16x8(y), qf);  // bf16 like the unfused path
-                } else {
-                    bf16x8_to_f32(qr, qf);
+                    rope_norm_row(a.rope_cs, kr, sub, hmask, hd.L - 1, true, y);
+                    new_k = f32_to_bf16x8(y);
                 }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) qf[e] *= a.scale_log2;
             }
             // Rows of this stage: half-warp `half` takes rows half, half + 2, ...
             const uint8_t* sk = smem + (size_t)s * stage_bytes + head_off_b;
             const uint8_t* sv = sk + (size_t)R * rowbytes;
-            // Operands come from shared memory (short latency), so two rows per half-warp per
-            // step are enough and keep the thread within 64 registers.
-            for (int r0 = 0; r0 < hd.nrows; r0 += 4) {
-                uint4 kr[2], vr[2];
-                bool valid[2];
+            // Each half-warp takes kRH rows per step (rows half, half + 2, ...), so that a step's
+            // dot products, shuffle reductions and exponentials are kRH independent chains and
+            // one online-softmax update covers 2 * kRH rows.  Four rows under the 576-thread
+            // register budget, two under the 1024-thread one.
+            constexpr int kRH = MAX_THREADS <= 576 ? 4 : 2;
+            for (int r0 = 0; r0 < hd.nrows; r0 += 2 * kRH) {
+                uint4 kr[kRH], vr[kRH];
+                bool valid[kRH];
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
+                for (int i = 0; i < kRH; ++i) {
                     const int r = r0 + 2 * i + half;
                     valid[i] = r < hd.nrows;
                     const int rr = valid[i] ? r : 0;
                     kr[i] = *reinterpret_cast<const uint4*>(sk + (size_t)rr * rowbytes);
                     vr[i] = *reinterpret_cast<const uint4*>(sv + (size_t)rr * rowbytes);
                 }
-                float sc[2];
+                float sc[kRH];
 #pragma unroll
-                for (int i = 0; i < 2; ++i) sc[i] = dot8(qf, kr[i]);
+                for (int i = 0; i < kRH; ++i) sc[i] = dot8(qf, kr[i]);
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
+                for (int i = 0; i < kRH; ++i) {
                     sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 8);
                     sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 4);
                     sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 2);
                     sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 1);
                     if (!valid[i]) sc[i] = kNegInf;
                 }
-                const float m_new = fmaxf(m, fmaxf(sc[0], sc[1]));
+                float bm = sc[0];
+#pragma unroll
+                for (int i = 1; i < kRH; ++i) bm = fmaxf(bm, sc[i]);
+                const float m_new = fmaxf(m, bm);
                 const float mu = (m_new == kNegInf) ? 0.f : m_new;
                 const float alpha = fast_exp2(m - mu);
-                const float p0 = fast_exp2(sc[0] - mu), p1 = fast_exp2(sc[1] - mu);
-                l = __fmaf_rn(l, alpha, p0 + p1);
-                float v0[8], v1[8];
-                bf16x8_to_f32(vr[0], v0);
-                bf16x8_to_f32(vr[1], v1);
+                float pr[kRH];
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    acc[e] = __fmaf_rn(p1, v1[e], __fmaf_rn(p0, v0[e], acc[e] * alpha));
+                for (int i = 0; i < kRH; ++i) pr[i] = fast_exp2(sc[i] - mu);
+                float psum = pr[0] + pr[1];
+                if (kRH == 4) psum += pr[2] + pr[3];
+                l = __fmaf_rn(l, alpha, psum);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] *= alpha;
+#pragma unroll
+                for (int i = 0; i < kRH; ++i) {
+                    float v[8];
+                    bf16x8_to_f32(vr[i], v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(pr[i], v[e], acc[e]);
+                }
                 m = m_new;
             }
             __syncwarp();
@@ -275,11 +325,8 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 const int pos = L - 1;
                 bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
                 bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
-                const uint4 kr = *reinterpret_cast<const uint4*>(a.k_new + qoff);
-                const uint4 vr = *reinterpret_cast<const uint4*>(a.v_new + qoff);
-                float y[8];
-                rope_norm_row(a.rope_cs, kr, sub, hmask, pos, true, y);
-                const uint4 kn = f32_to_bf16x8(y);
+                const uint4 kn = new_k;  // prepared at the start of this item
+                const uint4 vr = new_v;
                 const size_t coff = (size_t)pos * rowstride + (size_t)h * kHeadDim + 8 * sub;
                 if (half == 0) {
                     *reinterpret_cast<uint4*>(kb + coff) = kn;
@@ -346,36 +393,49 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
             __threadfence();
             if (lane == 0) *ctr = 0u;  // ready for the next launch
             const size_t base = (size_t)b * a.max_splits * H + h;
-            float M = kNegInf;
-            for (int sp = lane; sp < hd.n_splits; sp += 32)
+            const int ns = hd.n_splits;
+            // Lane j holds (max, sum) of splits j, j + 32, ...; the first group's stays in a
+            // register for the second pass.
+            float2 ml0 = make_float2(kNegInf, 0.f);
+            if (lane < ns) ml0 = __ldcg(a.part_ml + base + (size_t)lane * H);
+            float M = ml0.x;
+            for (int sp = lane + 32; sp < ns; sp += 32)
                 M = fmaxf(M, __ldcg(a.part_ml + base + (size_t)sp * H).x);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
             const float mu = (M == kNegInf) ? 0.f : M;
             float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int sp0 = 0; sp0 < hd.n_splits; sp0 += 4) {
-                float2 ml[4];
-                float4 v[4];
+            // kDepth partial outputs per round trip to L2 (fewer under the 1024-thread register
+            // budget); each split's weight comes from the lane that holds it.
+            constexpr int kDepth = MAX_THREADS <= 576 ? 8 : 4;
+            for (int g0 = 0; g0 < ns; g0 += 32) {
+                float2 ml = ml0;
+                if (g0 > 0)
+                    ml = g0 + lane < ns ? __ldcg(a.part_ml + base + (size_t)(g0 + lane) * H)
+                                        : make_float2(kNegInf, 0.f);
+                const float w = fast_exp2(ml.x - mu);  // 0 for a missing split (-inf)
+                float lw = ml.y * w;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int sp = sp0 + i;
-                    if (sp < hd.n_splits) {
-                        const size_t pi = base + (size_t)sp * H;
-                        ml[i] = __ldcg(a.part_ml + pi);
-                        v[i] = __ldcg(reinterpret_cast<const float4*>(a.part_o + pi * kHeadDim) + lane);
-                    } else {
-                        ml[i] = make_float2(kNegInf, 0.f);
-                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, o);
+                den += lw;
+                const int cnt = min(32, ns - g0);
+                for (int sp0 = 0; sp0 < cnt; sp0 += kDepth) {
+                    float4 v[kDepth];
+#pragma unroll
+                    for (int i = 0; i < kDepth; ++i) {
+                        const int sp = sp0 + i;
+                        v[i] = sp < cnt ? __ldcg(reinterpret_cast<const float4*>(
+                                              a.part_o + (base + (size_t)(g0 + sp) * H) * kHeadDim) + lane)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
-                }
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float w = fast_exp2(ml[i].x - mu);
-                    den = __fmaf_rn(ml[i].y, w, den);
-                    o4[0] = __fmaf_rn(v[i].x, w, o4[0]);
-                    o4[1] = __fmaf_rn(v[i].y, w, o4[1]);
-                    o4[2] = __fmaf_rn(v[i].z, w, o4[2]);
-                    o4[3] = __fmaf_rn(v[i].w, w, o4[3]);
+                    for (int i = 0; i < kDepth; ++i) {
+                        const float wi = __shfl_sync(0xFFFFFFFFu, w, (sp0 + i) & 31);
+                        o4[0] = __fmaf_rn(v[i].x, wi, o4[0]);
+                        o4[1] = __fmaf_rn(v[i].y, wi, o4[1]);
+                        o4[2] = __fmaf_rn(v[i].z, wi, o4[2]);
+                        o4[3] = __fmaf_rn(v[i].w, wi, o4[3]);
+                    }
                 }
             }
             const float inv = 1.0f / den;
