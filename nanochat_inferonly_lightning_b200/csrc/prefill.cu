@@ -13,14 +13,20 @@
 // boundaries, and the Q tile is double-buffered, so the next tile's loads and first QK MMAs
 // overlap the current tile's last blocks and epilogue.
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (320 threads, one CTA per SM):
 //   warp 0      TMA producers: lane 0 K(j) into a two-stage ring, lane 1 V(j) into a
 //               two-stage ring, lane 2 each tile's Q (two buffers).
 //   warp 1      allocates all 512 TMEM columns; one lane issues every tcgen05.mma.
-//   warps 2..5  softmax / epilogue: thread r owns query row r = TMEM lane r.
+//   warps 2..9  softmax / epilogue, two warps per TMEM lane quarter (warp w owns query rows
+//               32 * (w % 4) .. + 31 = its TMEM lanes): warps 2..5 take keys [0, 64) of every
+//               block ("half A"), warps 6..9 keys [64, 128) ("half B").  Each half keeps its own
+//               running max, row sum and output accumulator, so the two warps of a quarter never
+//               wait for each other inside a tile; they merge once, in the tile's epilogue.
+//               Two softmax warps per SMSP hide each other's latencies.
 // Tensor memory (512 columns): S0 [0,128) and S1 [128,256) hold Q.K^T of consecutive key
-// blocks (fp32); O [256,384) accumulates P.V (fp32); P0 [384,448) and P1 [448,512) hold the
-// bf16 probabilities (two per column) that feed the P.V MMA straight from TMEM.
+// blocks (fp32); O_A [256,384) and O_B [384,512) accumulate P.V of the two key halves (fp32).
+// Once a half has read its 64 S columns it writes its bf16 probabilities (two per column) over
+// the first 32 of them, where the P.V MMA reads them straight from TMEM.
 // Pipeline: the MMA warp keeps QK two blocks ahead of the softmax, so while the softmax of
 // block j+1 runs, the tensor pipe executes PV(j) and QK(j+2); the softmax warps go from one
 // block to the next without waiting for the tensor pipe.
@@ -43,13 +49,13 @@ namespace {
 
 constexpr int kBM = 128;             // query rows per CTA
 constexpr int kBN = 128;             // keys per block
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;      // producer warp, MMA warp, eight softmax warps
 constexpr uint32_t kBoxBytes = 64 * 128 * 2;    // one 64-dim x 128-row box, 128B swizzle
 constexpr uint32_t kTileBytes = 2 * kBoxBytes;  // 128 x 128 bf16
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;        // S0 at 0, S1 at 128
-constexpr uint32_t kColO = 256;
-constexpr uint32_t kColP = 384;      // P0 at 384, P1 at 448
+constexpr uint32_t kColS = 0;        // S0 at 0, S1 at 128; half h's P over [64h, 64h + 32) of S
+constexpr uint32_t kColOA = 256;     // O of key half A
+constexpr uint32_t kColOB = 384;     // O of key half B
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kNegInf = -__builtin_huge_valf();
 
@@ -59,22 +65,28 @@ enum Bar : int {
     kBarKFull = kBarQFree + 2,   // [2]
     kBarVFull = kBarKFull + 2,   // [2]
     kBarS = kBarVFull + 2,       // [2] QK(g) done: S(g & 1) full and K stage g & 1 free
-    kBarP = kBarS + 2,           // [2] softmax wrote P(g)
+    kBarP = kBarS + 2,           // [2] both halves wrote P(g) (256 arrivals)
     kBarPV = kBarP + 2,          // [2] PV(g) done: V stage free, P(g & 1) free
     kBarOFinal = kBarPV + 2,
-    kBarDrain = kBarOFinal + 1,  // the MMA warp's last commit: every MMA it issued is done
+    kBarXch = kBarOFinal + 1,    // [4] per lane quarter: both halves posted (max, sum) (64)
+    kBarXrd = kBarXch + 4,       // [4] per lane quarter: both halves read the other's (64)
+    kBarDrain = kBarXrd + 4,     // the MMA warp's last commit: every MMA it issued is done
     kNumBars
 };
 
 struct __align__(8) SmemTail {
     uint64_t bars[kNumBars];
+    float2 xch[4][2][32];  // per lane quarter and key half: each row's (max, sum) at the epilogue
     uint32_t tmem_base;
     int abort;
 };
 
 // Two Q buffers + two K stages + two V stages + the output staging tile.
 constexpr uint32_t kStageOutBytes = 128 * 128 * 2;  // 4 warps x (32 rows x 256 B)
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + 6 * kTileBytes + kStageOutBytes + sizeof(SmemTail);
+// No alignment slack: the dynamic shared memory window starts 1024-byte aligned (checked at
+// kernel entry), which the 128B-swizzled tiles need.
+constexpr size_t kSmemBytes = 6 * kTileBytes + kStageOutBytes + sizeof(SmemTail);
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 struct PrefillKParams {
     bf16* out;
@@ -177,13 +189,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                    const PrefillKParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // The budget has no room to realign: a window that is not 1024-byte aligned is reported
+    // and the kernel does nothing (uniform across the CTA, before any barrier or TMEM use).
+    if (smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0) atomicOr(p.status, kStatusBounds);
+        return;
+    }
+    uint8_t* smem = smem_raw;
     uint8_t* sQ = smem;                    // buffers at sQ, sQ + kTileBytes
     uint8_t* sK = smem + 2 * kTileBytes;   // stages at sK, sK + kTileBytes
     uint8_t* sV = smem + 4 * kTileBytes;   // stages at sV, sV + kTileBytes
-    uint8_t* sO = smem + 6 * kTileBytes;   // output staging, 8 KB per softmax warp
+    uint8_t* sO = smem + 6 * kTileBytes;   // output staging, 4 KB per softmax warp
     SmemTail* tail = reinterpret_cast<SmemTail*>(smem + 6 * kTileBytes + kStageOutBytes);
     uint64_t* bars = tail->bars;
     volatile int* abort_flag = &tail->abort;
@@ -193,7 +210,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i)
-            mbar_init(&bars[i], (i == kBarP || i == kBarP + 1) ? 128u : 1u);
+            mbar_init(&bars[i], (i == kBarP || i == kBarP + 1)         ? 256u
+                                : (i >= kBarXch && i < kBarXrd + 4) ? 64u
+                                                                    : 1u);
         tail->abort = 0;
         fence_mbar_init();
     }
@@ -347,20 +366,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!(ok = wait_all(kBarP + st, ph, 6))) break;
                 tc_fence_after();
                 const uint64_t dV = dV0 + st * kStageStep;
-                const uint32_t tp = tmem + kColP + st * 64;
-                const uint32_t acc0 = j > 0 ? 1u : 0u;  // first block of a tile starts O
+                const uint32_t tp = tmem + kColS + st * 128;  // P(g) lives in S slot g & 1
+                const uint32_t acc0 = j > 0 ? 1u : 0u;  // first block of a tile starts O_A, O_B
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    // 16 keys per PV step: P columns [8kk, 8kk+8) (bf16 pairs), V rows
-                    // [16kk, 16kk+16) = two 8-row swizzle groups.
-                    mma_ts_warp(tmem + kColO, tp + kk * 8, dV + kk * 128, idesc_pv,
-                                kk > 0 ? 1u : acc0);
+                for (int x = 0; x < 2; ++x) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // Key half x, 16 keys per step: P columns [64x + 8kk, +8) (bf16 pairs),
+                        // V rows [64x + 16kk, +16) = two 8-row swizzle groups, into O_x.
+                        mma_ts_warp(tmem + (x ? kColOB : kColOA), tp + 64 * x + 8 * kk,
+                                    dV + (4 * x + kk) * 128, idesc_pv, kk > 0 ? 1u : acc0);
+                    }
                 }
                 // The tile's output is complete once its last P.V is: the epilogue does not
                 // wait behind the next tile's QK.
                 if (j + 1 == nb) mma_commit_warp(&bars[kBarOFinal]);
-                // softmax(g) has read S(g & 1) (it wrote P(g) afterwards), so QK(g+2) may
-                // refill it.
+                // softmax(g) has read S(g & 1) and written P(g) over part of it; QK(g+2) refills
+                // the slot.  The tensor pipe executes one thread's MMAs in issue order, so
+                // QK(g+2) overwrites P(g) only after the P.V MMAs above have read it.
                 if (ahead.valid) {
                     if (!(ok = wait_qk_operands())) break;
                     tc_fence_after();
@@ -380,12 +403,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_drain(&bars[kBarDrain], 0, p.status, 13);
     } else {
         // ------------------------------------------------------------------ softmax / epilogue
+        // Warp w: lane quarter w % 4 (query rows = TMEM lanes), key half hx of every block.
         const int quarter = warp & 3;
+        const int hx = (warp - 2) >> 2;  // 0: keys [0, 64) of each block, 1: keys [64, 128)
         const int r = quarter * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        const uint32_t tO = tmem + kColO + lane_base;
+        const uint32_t tOA = tmem + kColOA + lane_base;
+        const uint32_t tOB = tmem + kColOB + lane_base;
+        const uint32_t tOx = hx ? tOB : tOA;  // this half's accumulator
         const float sl2 = p.scale_log2;
-        int g = 0, qi = 0;
+        int g = 0, qi = 0, xi = 0;
         bool ok = true;
         for (int k = 0; ok; ++k) {
             const int rank = tile_rank(k, blockIdx.x, gridDim.x);
@@ -393,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Tile t = make_tile(p, rank);
             const int q = t.q0 + r;
             const int qlim = q + t.off;  // last visible key for this row
-            float m_ref = kNegInf, l = 0.f;
+            float m_ref = kNegInf, l = 0.f;  // this half's running reference max and row sum
             for (int j = 0; j < t.nb; ++j, ++g) {
                 const int st = g & 1;
                 // Warp-uniform outcome: the TMEM accesses below are warp-collective.
@@ -403,41 +430,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const int key0 = j * kBN;
-                // Two ways through a block.  Exact: row max first, then the reference max is
-                // renewed (O and the row sum rescaled) if the block max exceeds it by more than
-                // the threshold, then P.  Optimistic: once every row of the warp has a finite
-                // reference, P is computed against it straight away; the block needed no renewal
-                // exactly when no P exceeds 2^threshold, which the block's row sum bounds (each
-                // P <= the sum), so a sum <= 2^threshold accepts the block and anything else
-                // (or NaN) redoes it the exact way.  After a tile's first block the optimistic
-                // path almost always holds and the max pass is skipped.
+                // This half's 64 scores: S slot st, columns [64hx, 64hx + 64) = keys
+                // key0 + 64hx + c.
+                const uint32_t sbase = tmem + kColS + st * 128 + 64 * hx + lane_base;
+                const int key0 = j * kBN + 64 * hx;
+                // Two ways through a block.  Exact: the half-row max first, then the reference
+                // max is renewed (this half's O and row sum rescaled) if the block max exceeds it
+                // by more than the threshold, then P.  Optimistic: once every row of the warp has
+                // a finite reference, P is computed against it straight away; no renewal was
+                // needed exactly when no P exceeds 2^threshold, which the half-block's row sum
+                // bounds (each P <= the sum), so a sum <= 2^threshold accepts the block and
+                // anything else (or NaN) redoes it the exact way.
                 const uint64_t sl2x2 = f2_pack(sl2, sl2);
                 uint64_t acc2[2];
-                uint32_t pk[64];
+                uint32_t pk[32];
                 bool exact = __any_sync(0xFFFFFFFFu, m_ref == kNegInf);
                 for (;;) {
-                    // S is (re)loaded from TMEM on each way through: it stays there until QK(g+2),
-                    // which waits for P(g), and reloading is cheaper than keeping 128 scores
-                    // live across a possible second pass.
-                    uint32_t sraw[128];
-                    tmem_ld128_sync(tmem + kColS + st * 128 + lane_base, sraw);
-                    float s[128];
+                    // S is (re)loaded from TMEM on each way through: it stays there until this
+                    // warp writes P over it, and reloading is cheaper than keeping 64 scores live
+                    // across a possible second pass.
+                    uint32_t sraw[64];
+                    tmem_ld64_sync(sbase, sraw);
+                    float s_[64];
 #pragma unroll
-                    for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sraw[c]);
-                    if (key0 + kBN - 1 > t.q0 + t.off || key0 + kBN > t.kv_len) {  // CTA-uniform
+                    for (int c = 0; c < 64; ++c) s_[c] = __uint_as_float(sraw[c]);
+                    if (key0 + 63 > t.q0 + t.off || key0 + 64 > t.kv_len) {  // CTA-uniform
                         const int lim = min(qlim + 1, t.kv_len) - key0;  // columns >= lim masked
 #pragma unroll
-                        for (int c = 0; c < 128; ++c) s[c] = c < lim ? s[c] : kNegInf;
+                        for (int c = 0; c < 64; ++c) s_[c] = c < lim ? s_[c] : kNegInf;
                     }
                     if (exact) {
-                        // Row max: 3-input max over pairs, eight independent chains.
+                        // Half-row max: 3-input max over pairs, eight independent chains.
                         float pm[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+                        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(s_[2 * i], s_[2 * i + 1]);
 #pragma unroll
-                        for (int c = 16; c < 128; c += 2)
-                            pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s[c], s[c + 1]);
+                        for (int c = 16; c < 64; c += 2)
+                            pm[(c >> 1) & 7] = fmax3(pm[(c >> 1) & 7], s_[c], s_[c + 1]);
                         const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
                                                fmaxf(pm[6], pm[7]));
                         const float bm2 = bm * sl2;
@@ -449,7 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             m_ref = bm2;
                         }
                         l *= alpha;
-                        // Rescale O for rows that renewed; O must first hold PV(g-1) complete.
+                        // Rescale this half's O for rows that renewed; it must first hold
+                        // PV(g-1) complete.
                         if (j > 0 && __any_sync(0xFFFFFFFFu, renew && alpha != 1.f)) {
                             const int sp = (g - 1) & 1;
                             if (!__all_sync(0xFFFFFFFFu,
@@ -462,11 +492,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
                                 uint32_t raw[32];
-                                tmem_ld32_sync(tO + 32 * c, raw);
+                                tmem_ld32_sync(tOx + 32 * c, raw);
 #pragma unroll
                                 for (int i = 0; i < 32; ++i)
                                     raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
-                                tmem_st32_sync(tO + 32 * c, raw);
+                                tmem_st32_sync(tOx + 32 * c, raw);
                             }
                         }
                     }
@@ -479,9 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc2[0] = f2_pack(0.f, 0.f);
                     acc2[1] = f2_pack(0.f, 0.f);
 #pragma unroll
-                    for (int i = 0; i < 64; ++i) {
+                    for (int i = 0; i < 32; ++i) {
                         float x0, x1, p0, p1;
-                        f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2x2, nmu2), x0, x1);
+                        f2_unpack(f2_fma(f2_pack(s_[2 * i], s_[2 * i + 1]), sl2x2, nmu2), x0, x1);
                         if ((i & 3) == 3) {
                             exp2_poly2(fminf(x0, 127.f), fminf(x1, 127.f), p0, p1);
                         } else {
@@ -504,69 +534,90 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float a0, a1, b0, b1;
                 f2_unpack(acc2[0], a0, a1);
                 f2_unpack(acc2[1], b0, b1);
-                // P(g & 1) was last read by PV(g-2).  No wait is needed: the MMA thread issued
-                // QK(g) after PV(g-2) and committed kBarS(g) after both, and a commit completes
-                // only when every earlier MMA of the issuing thread has, so the kBarS(g) wait
-                // above already covers PV(g-2).
-                tmem_st64_sync(tmem + kColP + st * 64 + lane_base, pk);
+                // P(g) goes over the first 32 of this half's S columns, which this warp has
+                // finished reading (every load above waited).  Their previous reader as P was
+                // PV(g-2); the MMA thread issued QK(g) after it and committed kBarS(g) after
+                // both, so the kBarS(g) wait above covers it.
+                tmem_st32_sync(sbase, pk);
                 l += (a0 + a1) + (b0 + b1);
                 tc_fence_before();
                 mbar_arrive(&bars[kBarP + st]);
             }
             if (!ok) break;
-            // Epilogue: O / l -> bf16 -> out[b, q, h, :].  The next tile's first PV (which
-            // overwrites O) waits for that tile's P, written only after these reads finish.
-            bf16* orow = p.out + (((size_t)t.b * p.seq_q + q) * p.heads + t.h) * kHeadDim;
+            // Epilogue: O = (O_A 2^(mA-M) + O_B 2^(mB-M)) / (lA 2^(mA-M) + lB 2^(mB-M)) -> bf16
+            // -> out[b, q, h, :]; this warp writes dims [64hx, 64hx + 64).  The next tile's first
+            // PV (which overwrites O_A and O_B) waits for that tile's P, written only after these
+            // reads finish.
+            bf16* orow = p.out + (((size_t)t.b * p.seq_q + q) * p.heads + t.h) * kHeadDim + 64 * hx;
             const bool store = q < p.seq_q;
             if (t.nb == 0) {
                 if (store) {
                     const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
+                    for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
                 }
                 continue;
             }
+            // Exchange (max, sum) with the other half's warp of this lane quarter: wait until it
+            // has read the previous tile's values, post ours, wait for its, read them, say so.
+            if (xi > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXrd + quarter], (xi - 1) & 1,
+                                                             abort_flag, p.status, 15))) {
+                ok = false;
+                break;
+            }
+            tail->xch[quarter][hx][lane] = make_float2(m_ref, l);
+            mbar_arrive(&bars[kBarXch + quarter]);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXch + quarter], xi & 1, abort_flag,
+                                                   p.status, 16))) {
+                ok = false;
+                break;
+            }
+            const float2 other = tail->xch[quarter][hx ^ 1][lane];
+            mbar_arrive(&bars[kBarXrd + quarter]);
+            ++xi;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarOFinal], qi & 1, abort_flag, p.status, 10))) {
                 ok = false;
                 break;
             }
             ++qi;
             tc_fence_after();
-            const float inv = 1.0f / l;  // l == 0 (no visible key) gives 0 * inf = NaN
-            // The warp stages its 32 rows in shared memory in the 128B-swizzled layout of a
-            // (64 dims x 32 rows) box, two boxes per row, and lane 0 writes them with two TMA
-            // stores: whole lines reach L2 instead of 32 scattered 16-byte pieces per store
-            // instruction.  The staging area is reused only after the previous stores from it
-            // have finished reading it.  Rows at or past seq_q are clipped by the tensor map.
-            uint8_t* stg = sO + quarter * 8192;
+            const float mA = hx ? other.x : m_ref, lA = hx ? other.y : l;
+            const float mB = hx ? m_ref : other.x, lB = hx ? l : other.y;
+            const float M = fmaxf(mA, mB);
+            const float muM = (M == kNegInf) ? 0.f : M;
+            const float wA = fast_exp2(mA - muM), wB = fast_exp2(mB - muM);  // 0 for -inf
+            const float inv = 1.0f / (lA * wA + lB * wB);  // no visible key: 0 * inf = NaN
+            const float fa = wA * inv, fb = wB * inv;
+            // The warp stages its 32 rows x 64 dims in shared memory in the 128B-swizzled
+            // layout of a (64 dims x 32 rows) box and lane 0 writes them with one TMA store:
+            // whole lines reach L2 instead of 32 scattered 16-byte pieces per store
+            // instruction.  The staging area is reused only after the previous store from it
+            // has finished reading it.  Rows at or past seq_q are clipped by the tensor map.
+            uint8_t* stg = sO + (quarter * 2 + hx) * 4096;
             if (lane == 0) bulk_wait_read_all();
             __syncwarp();
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t raw[32];
-                tmem_ld32_sync(tO + 32 * c, raw);
+            for (int c = 0; c < 2; ++c) {
+                uint32_t ra[32], rb[32];
+                tmem_ld32_sync(tOA + 64 * hx + 32 * c, ra);
+                tmem_ld32_sync(tOB + 64 * hx + 32 * c, rb);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    uint4 w;
-                    w.x = pack_bf16x2(__uint_as_float(raw[8 * i + 0]) * inv,
-                                      __uint_as_float(raw[8 * i + 1]) * inv);
-                    w.y = pack_bf16x2(__uint_as_float(raw[8 * i + 2]) * inv,
-                                      __uint_as_float(raw[8 * i + 3]) * inv);
-                    w.z = pack_bf16x2(__uint_as_float(raw[8 * i + 4]) * inv,
-                                      __uint_as_float(raw[8 * i + 5]) * inv);
-                    w.w = pack_bf16x2(__uint_as_float(raw[8 * i + 6]) * inv,
-                                      __uint_as_float(raw[8 * i + 7]) * inv);
-                    const int d = 32 * c + 8 * i;              // first of the 8 dims in w
-                    const int granule = ((d & 63) >> 3) ^ (lane & 7);  // 16-byte unit, swizzled
-                    *reinterpret_cast<uint4*>(stg + (d >> 6) * 4096 + lane * 128 + granule * 16) = w;
+                    float o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        o[e] = __fmaf_rn(__uint_as_float(ra[8 * i + e]), fa,
+                                         __uint_as_float(rb[8 * i + e]) * fb);
+                    const int d = 32 * c + 8 * i;           // first of the 8 dims (0..63)
+                    const int granule = (d >> 3) ^ (lane & 7);  // 16-byte unit, swizzled
+                    *reinterpret_cast<uint4*>(stg + lane * 128 + granule * 16) = f32_to_bf16x8(o);
                 }
             }
             fence_proxy_async_smem();
             __syncwarp();
             const int y0 = t.q0 + quarter * 32;
             if (lane == 0 && y0 < p.seq_q) {
-                tma_store_3d(&tmO, stg, t.h * 128, y0, t.b);
-                tma_store_3d(&tmO, stg + 4096, t.h * 128 + 64, y0, t.b);
+                tma_store_3d(&tmO, stg, t.h * 128 + 64 * hx, y0, t.b);
                 bulk_commit();
             }
             tc_fence_before();
