@@ -342,7 +342,7 @@ def bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic, e2e=True):
             "bound": "tensor", "achieved": flops_rank / (t_attn * 1e-3) / 1e12,
             "peak": peaks["tflops"], "unit": "TFLOP/s",
             "frac": flops_rank / (t_attn * 1e-3) / 1e12 / peaks["tflops"],
-            "traffic": traffic.get("prefill_kernel_cfg2"),
+            "traffic": traffic.get("prefill_kernel_cfg2") if impl.kind == "nc" else None,
             "kernel": "prefill_kernel (tcgen05)" if impl.kind == "nc" else "flash_attention_kernel",
             "peak_src": peaks["src"] + " bf16 burst",
         },
@@ -475,7 +475,8 @@ def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
         "bytes": W.decode_bytes(lens_all), "gpu_launches_per_step": launches,
         "timing": f"back-to-back steps over {R} rotating input set(s) (> 2x L2 in total)",
         "roofline": {"bound": "hbm", "achieved": rank_gbs, "peak": peaks["hbm"], "unit": "GB/s",
-                     "frac": rank_gbs / peaks["hbm"], "traffic": traffic.get(f"decode_kernel_{name}"),
+                     "frac": rank_gbs / peaks["hbm"],
+                     "traffic": traffic.get(f"decode_kernel_{name}") if impl.kind == "nc" else None,
                      "peak_src": peaks["src"]},
     }
 
