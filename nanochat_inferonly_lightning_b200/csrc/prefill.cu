@@ -33,7 +33,8 @@
 //
 // Softmax: fp32, base-2 exponentials of scale*log2(e)-scaled scores, with a lazily updated
 // reference max: O and the row sum are rescaled only when a block's max exceeds the
-// reference by more than 8 (log2 units).  Rows without any visible key produce NaN, as the
+// reference by more than 8 (log2 units).  The reference starts at the bound on the scores of
+// RMS-normalised q and k, so a tile's first block needs no max pass either.  Rows without any visible key produce NaN, as the
 // reference's 0/0 does.
 #include <cuda.h>
 
@@ -57,6 +58,9 @@ constexpr uint32_t kColS = 0;        // S0 at 0, S1 at 128; half h's P over [64h
 constexpr uint32_t kColOA = 256;     // O of key half A
 constexpr uint32_t kColOB = 384;     // O of key half B
 constexpr float kRescaleThreshold = 8.0f;
+// A tile's first block is accepted on the optimistic path only if its row sum is at least this
+// (below it the starting reference was far above the real max; the exact path resets it).
+constexpr float kMinFirstSum = 5.421010862427522e-20f;  // 2^-64
 constexpr float kNegInf = -__builtin_huge_valf();
 
 enum Bar : int {
@@ -412,6 +416,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tOB = tmem + kColOB + lane_base;
         const uint32_t tOx = hx ? tOB : tOA;  // this half's accumulator
         const float sl2 = p.scale_log2;
+        // Starting reference max: 128 |scale * log2(e)| bounds every score when q and k are
+        // RMS-normalised over 128 dims (|q.k| <= 128), as the fused RoPE + QK-norm pass leaves
+        // them.  A tile's first block then takes the optimistic path too.  For other inputs
+        // the optimistic checks fall back to the exact path: a block sum above 2^8 (scores
+        // above the bound), or on the first block one below 2^-64 (the bound far above them).
+        const float m_init = 128.f * fabsf(sl2);
         int g = 0, qi = 0, xi = 0;
         bool ok = true;
         for (int k = 0; ok; ++k) {
@@ -420,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const Tile t = make_tile(p, rank);
             const int q = t.q0 + r;
             const int qlim = q + t.off;  // last visible key for this row
-            float m_ref = kNegInf, l = 0.f;  // this half's running reference max and row sum
+            float m_ref = m_init, l = 0.f;  // this half's running reference max and row sum
             for (int j = 0; j < t.nb; ++j, ++g) {
                 const int st = g & 1;
                 // Warp-uniform outcome: the TMEM accesses below are warp-collective.
@@ -470,11 +480,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float bm = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
                                                fmaxf(pm[6], pm[7]));
                         const float bm2 = bm * sl2;
-                        const bool renew = (bm2 > m_ref + kRescaleThreshold) ||
+                        // On a tile's first block the reference is only the starting bound: it is
+                        // replaced by the block max (nothing has been accumulated yet).
+                        const bool renew = j == 0 || (bm2 > m_ref + kRescaleThreshold) ||
                                            (m_ref == kNegInf && bm2 != kNegInf);
                         float alpha = 1.f;
                         if (renew) {
-                            alpha = (m_ref == kNegInf) ? 0.f : fast_exp2(m_ref - bm2);
+                            alpha = (m_ref == kNegInf || j == 0) ? 0.f : fast_exp2(m_ref - bm2);
                             m_ref = bm2;
                         }
                         l *= alpha;
@@ -527,7 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     f2_unpack(acc2[1], d0, d1);
                     const float bsum = (c0 + c1) + (d0 + d1);
                     constexpr float kRenewSum = 256.0f;  // 2^kRescaleThreshold
-                    exact = __any_sync(0xFFFFFFFFu, !(bsum <= kRenewSum));
+                    exact = __any_sync(0xFFFFFFFFu, !(bsum <= kRenewSum) ||
+                                                        (j == 0 && !(bsum >= kMinFirstSum)));
                     if (!exact) break;
                 }
                 if (!ok) break;
