@@ -202,6 +202,13 @@ def test_flash_attention_prefill_wide_scores(nc):
     _attention_case(nc, None, 256, 640, 384, seed=99, qk_scale=3.0, normalise=False)
 
 
+def test_flash_attention_prefill_scores_far_below_bound(nc):
+    """A large softmax scale on RMS-normalised inputs: the kernel's starting reference max (the
+    bound 128 * scale * log2(e)) sits far above every block max, so a tile's first block has
+    a row sum below 2^-64 and is redone with its own max."""
+    _attention_case(nc, None, 256, 640, 384, seed=123, scale=0.5)
+
+
 def test_flash_attention_prefill_no_visible_key(nc):
     """kv_offset < 0: leading rows see no key and become NaN, like the reference's 0/0."""
     _attention_case(nc, None, 150, 150, -20, seed=5)
