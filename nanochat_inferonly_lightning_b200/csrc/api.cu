@@ -78,8 +78,11 @@ int status_word(int** out) {
     return NC_OK;
 }
 
-// Keys per split-KV chunk: aim for about four CTAs per SM over the whole batch.
+// Keys per split-KV chunk: for larger batches, aim for about four CTAs per SM over the whole
+// batch.
 int auto_split_len(int batch, int max_kv_len) {
+    // Small batches use the per-head layout (decode.cu), which takes 64 keys per split.
+    if (batch <= kDecodeHeadMaxBatch) return kDecodeHeadSplit;
     const long long est_keys = batch > 1 ? (long long)batch * max_kv_len / 2 : max_kv_len;
     const long long target = 148LL * 4;
     long long t = (est_keys + target - 1) / target;

@@ -448,6 +448,285 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
     __syncthreads();
 }
 
+// Per-head layout for small batches: one CTA of four warps per (split, head, sequence), at most
+// kDecodeHeadSplit = 64 keys per split.  Every warp issues the loads of its 16 rows at once,
+// straight into registers (a half-warp reads one row's 256 bytes of this head), so a split
+// costs one DRAM round trip and there is no queue or staging ring; with a few sequences this
+// puts work on every SM within one launch latency.  Same per-row arithmetic as decode_kernel
+// (fused RoPE + QK-norm of q and of the new key, online softmax in log2 units, four rows per
+// half-warp step); the four warps merge through shared memory, and, with several splits, the
+// last split of each (sequence, head) to finish combines them (per-head ticket, self-resetting).
+__global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
+    __shared__ float sm_o[4][kHeadDim];
+    __shared__ float2 sm_ml[4];
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int half = lane >> 4;
+    const int sub = lane & 15;
+    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+    const int H = a.heads;
+    const size_t rowstride = (size_t)H * kHeadDim;
+    const size_t qoff = (size_t)b * rowstride + (size_t)h * kHeadDim + 8 * sub;
+    // Independent loads first, so that they share one round trip: the sequence's length, its
+    // cache bases and this head's query.
+    const int Lraw = raw_len(a, b);
+    bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
+    bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
+    const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
+    const int L = min(Lraw, a.max_kv_len);
+    const int T = a.split_len;
+    const int n_splits = L > 0 ? (L + T - 1) / T : 1;
+    if (split >= n_splits) return;  // uniform across the CTA
+    if (split == 0 && h == 0 && threadIdx.x == 0 && Lraw > a.max_kv_len)
+        atomicOr(a.status, kStatusDecodeBound);
+    bf16* out_row = a.out + (size_t)b * rowstride + (size_t)h * kHeadDim;
+    if (L <= 0) {
+        // No visible key: the reference's 0/0 yields NaN (flash_attention.cu:155).
+        if (warp == 0 && half == 0)
+            *reinterpret_cast<uint4*>(out_row + 8 * sub) =
+                make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+        return;
+    }
+    const int ks = split * T;
+    const int ke = min(L, ks + T);
+    const bool owns_new = a.k_new != nullptr && ke == L;
+    const int ke_s = owns_new ? ke - 1 : ke;  // the new key comes from registers
+
+    // This warp's rows [w0, w1); half-warp `half` takes w0 + half, w0 + half + 2, ...
+    const int w0 = ks + 16 * warp;
+    const int w1 = min(ke_s, w0 + 16);
+    uint4 kr[8], vr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = w0 + 2 * i + half;
+        if (r < w1) {
+            const size_t off = (size_t)r * rowstride + (size_t)h * kHeadDim + 8 * sub;
+            kr[i] = *reinterpret_cast<const uint4*>(kb + off);
+            vr[i] = *reinterpret_cast<const uint4*>(vb + off);
+        } else {
+            kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    float qf[8];
+    {
+        if (a.q_raw) {
+            float y[8];
+            rope_norm_row(a.rope_cs, qr, sub, hmask, L - 1, true, y);
+            bf16x8_to_f32(f32_to_bf16x8(y), qf);  // bf16 like the unfused path
+        } else {
+            bf16x8_to_f32(qr, qf);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qf[e] *= a.scale_log2;
+    }
+    // New token (position L-1), warp 0 of the CTA that owns it: RoPE + QK-norm of its key,
+    // append K and V to the cache (lanes of half 0), add its contribution below.
+    uint4 new_k = make_uint4(0u, 0u, 0u, 0u), new_v = new_k;
+    if (owns_new && warp == 0) {
+        const uint4 kraw = *reinterpret_cast<const uint4*>(a.k_new + qoff);
+        new_v = *reinterpret_cast<const uint4*>(a.v_new + qoff);
+        float y[8];
+        rope_norm_row(a.rope_cs, kraw, sub, hmask, L - 1, true, y);
+        new_k = f32_to_bf16x8(y);
+        const size_t coff = (size_t)(L - 1) * rowstride + (size_t)h * kHeadDim + 8 * sub;
+        if (half == 0) {
+            *reinterpret_cast<uint4*>(kb + coff) = new_k;
+            *reinterpret_cast<uint4*>(vb + coff) = new_v;
+        }
+    }
+
+    float m = kNegInf, l = 0.f, acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int s4 = 0; s4 < 2; ++s4) {
+        float sc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int idx = 4 * s4 + i;
+            sc[i] = dot8(qf, kr[idx]);
+            sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 8);
+            sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 4);
+            sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 2);
+            sc[i] += __shfl_xor_sync(0xFFFFFFFFu, sc[i], 1);
+            if (!(w0 + 2 * idx + half < w1)) sc[i] = kNegInf;
+        }
+        const float bm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        const float m_new = fmaxf(m, bm);
+        const float mu = (m_new == kNegInf) ? 0.f : m_new;
+        const float alpha = fast_exp2(m - mu);
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pr[i] = fast_exp2(sc[i] - mu);
+        l = __fmaf_rn(l, alpha, (pr[0] + pr[1]) + (pr[2] + pr[3]));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] *= alpha;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float v[8];
+            bf16x8_to_f32(vr[4 * s4 + i], v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(pr[i], v[e], acc[e]);
+        }
+        m = m_new;
+    }
+    if (owns_new && warp == 0) {
+        float sc = dot8(qf, new_k);
+        sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 8);
+        sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 4);
+        sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 2);
+        sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 1);
+        if (half == 0) {
+            const float m_new = fmaxf(m, sc);
+            const float alpha = fast_exp2(m - m_new);
+            const float pr = fast_exp2(sc - m_new);
+            l = __fmaf_rn(l, alpha, pr);
+            float v[8];
+            bf16x8_to_f32(new_v, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(pr, v[e], acc[e] * alpha);
+            m = m_new;
+        }
+    }
+    // Merge the two half-warps (same dims, disjoint keys), then the four warps.
+    {
+        const float m_o = __shfl_xor_sync(0xFFFFFFFFu, m, 16);
+        const float l_o = __shfl_xor_sync(0xFFFFFFFFu, l, 16);
+        const float M = fmaxf(m, m_o);
+        const float mu = (M == kNegInf) ? 0.f : M;
+        const float wa = fast_exp2(m - mu), wb = fast_exp2(m_o - mu);
+        l = l * wa + l_o * wb;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float o = __shfl_xor_sync(0xFFFFFFFFu, acc[e], 16);
+            acc[e] = acc[e] * wa + o * wb;
+        }
+        m = M;
+    }
+    if (half == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sm_o[warp][8 * sub + e] = acc[e];
+    }
+    if (lane == 0) sm_ml[warp] = make_float2(m, l);
+    __syncthreads();
+    if (warp != 0) return;
+    // Warp 0: lane owns dims [4*lane, 4*lane+4).
+    float M = kNegInf;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w].x);
+    const float mu = (M == kNegInf) ? 0.f : M;
+    float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float wt = fast_exp2(sm_ml[w].x - mu);
+        den = __fmaf_rn(sm_ml[w].y, wt, den);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o4[i] = __fmaf_rn(sm_o[w][4 * lane + i], wt, o4[i]);
+    }
+    if (n_splits == 1) {
+        const float inv = 1.0f / den;
+        uint2 r;
+        r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
+        r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
+        *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
+        return;
+    }
+    // Partial result of this split (max, sum, unnormalised output), then the ticket.
+    const size_t pidx = ((size_t)b * a.max_splits + split) * H + h;
+    __stcg(reinterpret_cast<float4*>(a.part_o + pidx * kHeadDim) + lane,
+           make_float4(o4[0], o4[1], o4[2], o4[3]));
+    if (lane == 0) __stcg(a.part_ml + pidx, make_float2(M, den));
+    __threadfence();
+    __syncwarp();
+    unsigned ticket = 0;
+    unsigned* ctr = a.counters + kQueueWords + (size_t)b * H + h;
+    if (lane == 0) ticket = atomicAdd(ctr, 1u);
+    ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+    if (ticket != (unsigned)(n_splits - 1)) return;
+    // Last split of (b, h): combine.
+    __threadfence();
+    if (lane == 0) *ctr = 0u;  // ready for the next launch
+    const size_t base = (size_t)b * a.max_splits * H + h;
+    if (n_splits <= 8) {
+        // Up to 8 splits (up to 512 keys): every partial is loaded in one round trip.
+        float4 v[8];
+        float2 ml[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const bool ok = i < n_splits;
+            v[i] = ok ? __ldcg(reinterpret_cast<const float4*>(
+                           a.part_o + (base + (size_t)i * H) * kHeadDim) + lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            ml[i] = ok ? __ldcg(a.part_ml + base + (size_t)i * H) : make_float2(kNegInf, 0.f);
+        }
+        float Mf = kNegInf;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) Mf = fmaxf(Mf, ml[i].x);
+        const float muf = (Mf == kNegInf) ? 0.f : Mf;
+        float df = 0.f, of[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float w = fast_exp2(ml[i].x - muf);
+            df = __fmaf_rn(ml[i].y, w, df);
+            of[0] = __fmaf_rn(v[i].x, w, of[0]);
+            of[1] = __fmaf_rn(v[i].y, w, of[1]);
+            of[2] = __fmaf_rn(v[i].z, w, of[2]);
+            of[3] = __fmaf_rn(v[i].w, w, of[3]);
+        }
+        const float invf = 1.0f / df;
+        uint2 rf;
+        rf.x = pack_bf16x2(of[0] * invf, of[1] * invf);
+        rf.y = pack_bf16x2(of[2] * invf, of[3] * invf);
+        *reinterpret_cast<uint2*>(out_row + 4 * lane) = rf;
+        return;
+    }
+    float2 ml0 = make_float2(kNegInf, 0.f);
+    if (lane < n_splits) ml0 = __ldcg(a.part_ml + base + (size_t)lane * H);
+    float Mc = ml0.x;
+    for (int sp = lane + 32; sp < n_splits; sp += 32)
+        Mc = fmaxf(Mc, __ldcg(a.part_ml + base + (size_t)sp * H).x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xFFFFFFFFu, Mc, o));
+    const float muc = (Mc == kNegInf) ? 0.f : Mc;
+    float dc = 0.f, oc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int g0 = 0; g0 < n_splits; g0 += 32) {
+        float2 ml = ml0;
+        if (g0 > 0)
+            ml = g0 + lane < n_splits ? __ldcg(a.part_ml + base + (size_t)(g0 + lane) * H)
+                                      : make_float2(kNegInf, 0.f);
+        const float w = fast_exp2(ml.x - muc);
+        float lw = ml.y * w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, o);
+        dc += lw;
+        const int cnt = min(32, n_splits - g0);
+        for (int sp0 = 0; sp0 < cnt; sp0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int sp = sp0 + i;
+                v[i] = sp < cnt ? __ldcg(reinterpret_cast<const float4*>(
+                                      a.part_o + (base + (size_t)(g0 + sp) * H) * kHeadDim) + lane)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float wi = __shfl_sync(0xFFFFFFFFu, w, (sp0 + i) & 31);
+                oc[0] = __fmaf_rn(v[i].x, wi, oc[0]);
+                oc[1] = __fmaf_rn(v[i].y, wi, oc[1]);
+                oc[2] = __fmaf_rn(v[i].z, wi, oc[2]);
+                oc[3] = __fmaf_rn(v[i].w, wi, oc[3]);
+            }
+        }
+    }
+    const float inv = 1.0f / dc;
+    uint2 r;
+    r.x = pack_bf16x2(oc[0] * inv, oc[1] * inv);
+    r.y = pack_bf16x2(oc[2] * inv, oc[3] * inv);
+    *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
+}
+
 }  // namespace
 
 // Rows per ring stage for a head count: three stages of K and V rows within ~216 KB.
@@ -497,6 +776,11 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
+    }
+    if (a.batch <= kDecodeHeadMaxBatch && a.split_len <= kDecodeHeadSplit) {
+        decode_head_kernel<<<dim3((unsigned)a.max_splits, (unsigned)a.heads, (unsigned)a.batch),
+                             128, 0, stream>>>(a);
+        return cudaGetLastError();
     }
     const long long items = (long long)a.max_splits * a.batch;
     const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(items, sms[dev]));

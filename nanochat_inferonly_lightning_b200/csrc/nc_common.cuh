@@ -214,6 +214,10 @@ struct DecodeArgs {
 };
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
+// Small batches (<= 8 sequences) run the per-head decode layout: one CTA per (split, head,
+// sequence) with at most kDecodeHeadSplit keys per split.
+constexpr int kDecodeHeadMaxBatch = 8;
+constexpr int kDecodeHeadSplit = 64;
 size_t decode_workspace_bytes(int batch, int max_splits, int heads);
 // 32-bit words at the start of the decode workspace: two work-queue words, then one split
 // ticket per (sequence, head).  All zero between launches.

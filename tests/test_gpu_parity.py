@@ -284,6 +284,12 @@ def test_decode_batched_unfused(nc):
     _decode_batch(nc, [3, 64, 65, 700], 0, seed=400, fused=False)
 
 
+def test_decode_batched_streaming_layout(nc):
+    """More than 8 sequences: the streaming layout (all heads of a split per work item, CTAs
+    taking items from a queue), with automatic splits."""
+    _decode_batch(nc, [1, 5, 16, 33, 64, 128, 300, 511, 777, 1024, 1500, 2047], 0, seed=450)
+
+
 def test_decode_cfg3_lengths_subset(nc):
     """First 8 sequences of cfg3's kv_len draw (torch seed 2)."""
     from nanochat_inferonly_lightning_b200 import workloads
