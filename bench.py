@@ -19,7 +19,8 @@ host's launches of all K steps, keeps host launch latency out of the device timi
 attention kernel and the RoPE/append pass are also timed on their own, the same way, for the
 roofline.  `e2e` repeats the headline through the public API from pinned host
 buffers with the host->device copies of Q/K/V and the device->host copy of the output inside
-the timed region.
+the timed region, successive steps alternating between two streams so that copies overlap
+kernels.
 
 --impl reference runs the same workloads through the reference's own CUDA kernels
 (kernels/rope.cu + kernels/flash_attention.cu rebuilt for sm_100a, oracle/_ref) and the
@@ -348,45 +349,61 @@ def bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic, e2e=True):
         },
     }
     if e2e:
-        q, k, v, kc, vc, out = sets[0]
-        res["e2e"] = bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0, kc, vc, out)
+        res["e2e"] = bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0)
     return res
 
 
-def bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0, kc, vc, out):
-    """Same step through the public API from pinned host buffers: H2D of Q/K/V, the attention
-    path, D2H of the output, all inside the timed region."""
+def bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0):
+    """Same step through the public API from pinned host buffers: every step copies its Q/K/V
+    host->device, runs the attention path and copies its output device->host, all inside the
+    timed region.  Successive steps alternate between two CUDA streams, each with its own
+    device buffers, so one step's host->device copy overlaps the previous step's kernels and
+    its device->host copy (the copy engines and the SMs work at the same time; the host link
+    is the bound)."""
     S = W.CFG2_SEQ
     hq, hk, hv = (t.cpu().pin_memory() for t in (q0, k0, v0))
-    hout = torch.empty((S, ROW), dtype=torch.bfloat16).pin_memory()
-    q = torch.empty_like(q0)
-    k = torch.empty_like(k0)
-    v = torch.empty_like(v0)
+    lanes = []
+    for _ in range(2):
+        kc = torch.zeros((S, H, D), dtype=torch.bfloat16, device="cuda")
+        lanes.append((torch.cuda.Stream(), torch.empty_like(q0), torch.empty_like(k0),
+                      torch.empty_like(v0), kc, torch.zeros_like(kc),
+                      torch.empty((S, ROW), dtype=torch.bfloat16, device="cuda"),
+                      torch.empty((S, ROW), dtype=torch.bfloat16).pin_memory()))
+    it = [0]
 
     def step():
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        impl.prefill_step(out, q, k, v, kc, vc, S, 0)
-        hout.copy_(out, non_blocking=True)
+        st, q, k, v, kc, vc, out, hout = lanes[it[0] % 2]
+        it[0] += 1
+        with torch.cuda.stream(st):
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            impl.prefill_step(out, q, k, v, kc, vc, S, 0)
+            hout.copy_(out, non_blocking=True)
 
     for _ in range(Wm):
         step()
     torch.cuda.synchronize()
     dist.barrier()
+    main = torch.cuda.current_stream()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    s.record()
+    s.record(main)
+    for ln in lanes:
+        ln[0].wait_stream(main)
     for _ in range(K):
         step()
-    e.record()
+    for ln in lanes:
+        main.wait_stream(ln[0])
+    e.record(main)
     torch.cuda.synchronize()
     dist.barrier()
     t = dist.max(s.elapsed_time(e) / K)
     bi = 3 * S * ROW * 2
     bo = S * ROW * 2
     return {"value": dist.sum(W.CFG2_FLOPS) / (t * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": t, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+            "ms_per_step": t, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+            "pipelining": "steps alternate between two CUDA streams (copies overlap kernels)"}
 
 
 def build_decode_batch(impl, lens, seed):
