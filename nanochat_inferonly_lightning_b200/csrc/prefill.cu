@@ -424,12 +424,97 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_init = 128.f * fabsf(sl2);
         int g = 0, qi = 0, xi = 0;
         bool ok = true;
+        // Epilogue of a tile: O = (O_A 2^(mA-M) + O_B 2^(mB-M)) / (lA 2^(mA-M) + lB 2^(mB-M))
+        // -> bf16 -> out[b, q, h, :]; this warp writes dims [64hx, 64hx + 64).  Run between
+        // the next tile's first P store and its arrive (or after the last tile): the next
+        // tile's first PV, which overwrites O_A and O_B, waits for that arrive, and the wait for
+        // this tile's last PV overlaps the next tile's first softmax block.
+        auto finish_tile = [&](const Tile& t, float m_ref, float l) -> bool {
+            // Exchange (max, sum) with the other half's warp of this lane quarter: wait until it
+            // has read the previous tile's values, post ours, wait for its, read them, say so.
+            if (xi > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXrd + quarter], (xi - 1) & 1,
+                                                             abort_flag, p.status, 15))) {
+                return false;
+            }
+            tail->xch[quarter][hx][lane] = make_float2(m_ref, l);
+            mbar_arrive(&bars[kBarXch + quarter]);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXch + quarter], xi & 1, abort_flag,
+                                                   p.status, 16))) {
+                return false;
+            }
+            const float2 other = tail->xch[quarter][hx ^ 1][lane];
+            mbar_arrive(&bars[kBarXrd + quarter]);
+            ++xi;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarOFinal], qi & 1, abort_flag, p.status, 10))) {
+                return false;
+            }
+            ++qi;
+            tc_fence_after();
+            const float mA = hx ? other.x : m_ref, lA = hx ? other.y : l;
+            const float mB = hx ? m_ref : other.x, lB = hx ? l : other.y;
+            const float M = fmaxf(mA, mB);
+            const float muM = (M == kNegInf) ? 0.f : M;
+            const float wA = fast_exp2(mA - muM), wB = fast_exp2(mB - muM);  // 0 for -inf
+            const float inv = 1.0f / (lA * wA + lB * wB);  // no visible key: 0 * inf = NaN
+            const float fa = wA * inv, fb = wB * inv;
+            // The warp stages its 32 rows x 64 dims in shared memory in the 128B-swizzled
+            // layout of a (64 dims x 32 rows) box and lane 0 writes them with one TMA store:
+            // whole lines reach L2 instead of 32 scattered 16-byte pieces per store
+            // instruction.  The staging area is reused only after the previous store from it
+            // has finished reading it.  Rows at or past seq_q are clipped by the tensor map.
+            uint8_t* stg = sO + (quarter * 2 + hx) * 4096;
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+    #pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t ra[32], rb[32];
+                tmem_ld32_sync(tOA + 64 * hx + 32 * c, ra);
+                tmem_ld32_sync(tOB + 64 * hx + 32 * c, rb);
+    #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float o[8];
+    #pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        o[e] = __fmaf_rn(__uint_as_float(ra[8 * i + e]), fa,
+                                         __uint_as_float(rb[8 * i + e]) * fb);
+                    const int d = 32 * c + 8 * i;           // first of the 8 dims (0..63)
+                    const int granule = (d >> 3) ^ (lane & 7);  // 16-byte unit, swizzled
+                    *reinterpret_cast<uint4*>(stg + lane * 128 + granule * 16) = f32_to_bf16x8(o);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            const int y0 = t.q0 + quarter * 32;
+            if (lane == 0 && y0 < p.seq_q) {
+                tma_store_3d(&tmO, stg, t.h * 128 + 64 * hx, y0, t.b);
+                bulk_commit();
+            }
+            tc_fence_before();
+            return true;
+        };
+        bool pend = false;  // a finished tile whose epilogue has not run yet: pt, pm, pl
+        Tile pt{};
+        float pm = 0.f, pl = 0.f;
         for (int k = 0; ok; ++k) {
             const int rank = tile_rank(k, blockIdx.x, gridDim.x);
             if (rank >= p.total_tiles) break;
             const Tile t = make_tile(p, rank);
             const int q = t.q0 + r;
             const int qlim = q + t.off;  // last visible key for this row
+            if (t.nb == 0) {
+                // No visible key for any row of the tile: NaN, like the reference's 0/0.
+                if (pend) {
+                    if (!(ok = finish_tile(pt, pm, pl))) break;
+                    pend = false;
+                }
+                if (q < p.seq_q) {
+                    bf16* orow = p.out + (((size_t)t.b * p.seq_q + q) * p.heads + t.h) * kHeadDim + 64 * hx;
+                    const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
+                }
+                continue;
+            }
             float m_ref = m_init, l = 0.f;  // this half's running reference max and row sum
             for (int j = 0; j < t.nb; ++j, ++g) {
                 const int st = g & 1;
@@ -553,88 +638,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // both, so the kBarS(g) wait above covers it.
                 tmem_st32_sync(sbase, pk);
                 l += (a0 + a1) + (b0 + b1);
+                if (j == 0 && pend) {
+                    if (!(ok = finish_tile(pt, pm, pl))) break;
+                    pend = false;
+                }
                 tc_fence_before();
                 mbar_arrive(&bars[kBarP + st]);
             }
             if (!ok) break;
-            // Epilogue: O = (O_A 2^(mA-M) + O_B 2^(mB-M)) / (lA 2^(mA-M) + lB 2^(mB-M)) -> bf16
-            // -> out[b, q, h, :]; this warp writes dims [64hx, 64hx + 64).  The next tile's first
-            // PV (which overwrites O_A and O_B) waits for that tile's P, written only after these
-            // reads finish.
-            bf16* orow = p.out + (((size_t)t.b * p.seq_q + q) * p.heads + t.h) * kHeadDim + 64 * hx;
-            const bool store = q < p.seq_q;
-            if (t.nb == 0) {
-                if (store) {
-                    const uint4 nan4 = make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) reinterpret_cast<uint4*>(orow)[i] = nan4;
-                }
-                continue;
-            }
-            // Exchange (max, sum) with the other half's warp of this lane quarter: wait until it
-            // has read the previous tile's values, post ours, wait for its, read them, say so.
-            if (xi > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXrd + quarter], (xi - 1) & 1,
-                                                             abort_flag, p.status, 15))) {
-                ok = false;
-                break;
-            }
-            tail->xch[quarter][hx][lane] = make_float2(m_ref, l);
-            mbar_arrive(&bars[kBarXch + quarter]);
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarXch + quarter], xi & 1, abort_flag,
-                                                   p.status, 16))) {
-                ok = false;
-                break;
-            }
-            const float2 other = tail->xch[quarter][hx ^ 1][lane];
-            mbar_arrive(&bars[kBarXrd + quarter]);
-            ++xi;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars[kBarOFinal], qi & 1, abort_flag, p.status, 10))) {
-                ok = false;
-                break;
-            }
-            ++qi;
-            tc_fence_after();
-            const float mA = hx ? other.x : m_ref, lA = hx ? other.y : l;
-            const float mB = hx ? m_ref : other.x, lB = hx ? l : other.y;
-            const float M = fmaxf(mA, mB);
-            const float muM = (M == kNegInf) ? 0.f : M;
-            const float wA = fast_exp2(mA - muM), wB = fast_exp2(mB - muM);  // 0 for -inf
-            const float inv = 1.0f / (lA * wA + lB * wB);  // no visible key: 0 * inf = NaN
-            const float fa = wA * inv, fb = wB * inv;
-            // The warp stages its 32 rows x 64 dims in shared memory in the 128B-swizzled
-            // layout of a (64 dims x 32 rows) box and lane 0 writes them with one TMA store:
-            // whole lines reach L2 instead of 32 scattered 16-byte pieces per store
-            // instruction.  The staging area is reused only after the previous store from it
-            // has finished reading it.  Rows at or past seq_q are clipped by the tensor map.
-            uint8_t* stg = sO + (quarter * 2 + hx) * 4096;
-            if (lane == 0) bulk_wait_read_all();
-            __syncwarp();
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t ra[32], rb[32];
-                tmem_ld32_sync(tOA + 64 * hx + 32 * c, ra);
-                tmem_ld32_sync(tOB + 64 * hx + 32 * c, rb);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float o[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        o[e] = __fmaf_rn(__uint_as_float(ra[8 * i + e]), fa,
-                                         __uint_as_float(rb[8 * i + e]) * fb);
-                    const int d = 32 * c + 8 * i;           // first of the 8 dims (0..63)
-                    const int granule = (d >> 3) ^ (lane & 7);  // 16-byte unit, swizzled
-                    *reinterpret_cast<uint4*>(stg + lane * 128 + granule * 16) = f32_to_bf16x8(o);
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            const int y0 = t.q0 + quarter * 32;
-            if (lane == 0 && y0 < p.seq_q) {
-                tma_store_3d(&tmO, stg, t.h * 128 + 64 * hx, y0, t.b);
-                bulk_commit();
-            }
-            tc_fence_before();
+            pend = true;
+            pt = t;
+            pm = m_ref;
+            pl = l;
         }
+        if (ok && pend) ok = finish_tile(pt, pm, pl);
         // Output stores still reading the staging tile must finish before the CTA exits.
         if (lane == 0) bulk_wait_all();
         __syncwarp();
