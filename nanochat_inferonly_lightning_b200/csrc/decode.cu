@@ -777,7 +777,7 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    if (a.batch <= kDecodeHeadMaxBatch && a.split_len <= kDecodeHeadSplit) {
+    if (a.head_layout) {
         decode_head_kernel<<<dim3((unsigned)a.max_splits, (unsigned)a.heads, (unsigned)a.batch),
                              128, 0, stream>>>(a);
         return cudaGetLastError();

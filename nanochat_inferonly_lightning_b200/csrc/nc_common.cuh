@@ -204,6 +204,7 @@ struct DecodeArgs {
     int batch;
     int heads;
     int q_raw;                    // 1: q is pre-RoPE and gets RoPE + QK-norm in the kernel
+    int head_layout;              // 1: per-head layout (decode_use_head_layout)
     float scale_log2;             // softmax scale * log2(e)
     int split_len;                // keys per split (multiple of 16)
     int max_splits;
@@ -214,10 +215,19 @@ struct DecodeArgs {
 };
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
-// Small batches (<= 8 sequences) run the per-head decode layout: one CTA per (split, head,
-// sequence) with at most kDecodeHeadSplit keys per split.
+// Small decode calls run the per-head layout: one CTA per (split, head, sequence) with at
+// most kDecodeHeadSplit keys per split.  It is chosen for at most kDecodeHeadMaxBatch sequences
+// and, with automatic splits, at most kDecodeHeadMaxKeys keys in total (batch * max_kv_len);
+// above that the streaming layout reaches more of the HBM bandwidth (measured at 8 x 1024
+// keys).  An explicit split length above kDecodeHeadSplit selects the streaming layout.
 constexpr int kDecodeHeadMaxBatch = 8;
 constexpr int kDecodeHeadSplit = 64;
+constexpr long long kDecodeHeadMaxKeys = 4096;
+inline bool decode_use_head_layout(int batch, int max_kv_len, int split_len) {
+    if (batch > kDecodeHeadMaxBatch) return false;
+    if (split_len) return split_len <= kDecodeHeadSplit;
+    return (long long)batch * max_kv_len <= kDecodeHeadMaxKeys;
+}
 size_t decode_workspace_bytes(int batch, int max_splits, int heads);
 // 32-bit words at the start of the decode workspace: two work-queue words, then one split
 // ticket per (sequence, head).  All zero between launches.
