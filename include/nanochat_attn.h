@@ -176,6 +176,37 @@ int nc_kv_cache_prefill(nc_kv_cache* cache, int layer, int seq, void* out, void*
 int nc_kv_cache_decode(nc_kv_cache* cache, int layer, void* out, const void* q,
                        const void* k_new, const void* v_new, float scale, cudaStream_t stream);
 
+/* ----------------------------------------------------------------------------------------
+ * Skinny GEMM for the decode step: out[M, N] = epilogue(x[M, K] . w[N, K]^T) for 1 <= M <= 64
+ * rows (one per sequence of a decode batch), bf16 operands, fp32 accumulation on the tcgen05
+ * tensor cores, one bf16 rounding of the result.  w is a weight in the reference layout
+ * W[out, in] and is streamed from HBM once; the K dimension is split across up to 8 CTAs of one
+ * thread-block cluster when N alone gives too few tiles (partials are summed through
+ * distributed shared memory in a fixed order: results are deterministic, no workspace).
+ * Optional steps, chosen by `flags`, are fused so that each replaces a separate pass:
+ *   NC_GEMM_NORM_INPUT  the product is scaled per row by rsqrt(mean(x[m,:]^2) + 1e-6), i.e.
+ *                       the GEMM consumes RMSNorm(x) (kernels/rmsnorm.cu:9-56) without it
+ *                       being materialised;
+ *   NC_GEMM_RESIDUAL    + residual[m, n] ([M, N] bf16; may equal out), as gemm_half_residual;
+ *   NC_GEMM_RELU2       relu(v)^2 (kernels/ops.cu:23-30);
+ *   NC_GEMM_TANH_CAP    cap * tanh(v / cap) (kernels/ops.cu:39-46), with cap = `cap`.
+ * Order: scale, residual, relu^2, tanh cap.  `seg_cols` (0 = N) splits the output into
+ * N / seg_cols segments stored one after another, each [M, seg_cols]: a fused Q|K|V weight
+ * then writes q, k and v as three separate [M, 2176] arrays.
+ * Requirements: K % 8 == 0; x and w 16-byte aligned; out must not overlap x; `splits` 0 picks
+ * the split count, else that many (clamped to [1, 8] and to the number of 64-wide K blocks).
+ * Replaces: gemm_half / gemm_half_residual for M <= 16 (kernels/gemm.cu:62-166, the small-M
+ * branch) at the decode call sites src/model.cpp:114-116, :139, :149-150, :153, :174-177,
+ * together with the rmsnorm / relu_squared / tanh_cap launches around them. */
+enum {
+    NC_GEMM_NORM_INPUT = 1,
+    NC_GEMM_RESIDUAL = 2,
+    NC_GEMM_RELU2 = 4,
+    NC_GEMM_TANH_CAP = 8
+};
+int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual, int M, int N,
+                   int K, int flags, float cap, int seg_cols, int splits, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

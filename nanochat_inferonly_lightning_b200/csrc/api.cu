@@ -281,6 +281,7 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
 
 int internal_rope_table(const float2** table) { return ensure_rope(table); }
 int internal_status_word(int** status) { return status_word(status); }
+int internal_cuda_fail(cudaError_t e) { return cuda_fail(e); }
 
 }  // namespace nc
 

@@ -76,6 +76,10 @@ __device__ __forceinline__ int raw_len(const DecodeArgs& a, int b) {
 // MAX_THREADS selects the register budget: (heads + 1) warps must fit in it.
 template <int MAX_THREADS>
 __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, int rows_per_stage) {
+    // A GEMM launched after this kernel with programmatic dependent launch (the output
+    // projection) may start streaming its weights now; it waits for this grid to complete
+    // before it reads anything this kernel writes.
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -457,6 +461,7 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
 // half-warp step); the four warps merge through shared memory, and, with several splits, the
 // last split of each (sequence, head) to finish combines them (per-head ticket, self-resetting).
 __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;");  // as in decode_kernel
     __shared__ float sm_o[4][kHeadDim];
     __shared__ float2 sm_ml[4];
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;

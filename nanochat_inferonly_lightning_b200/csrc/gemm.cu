@@ -1,0 +1,487 @@
+// Skinny bf16 GEMM for the decode step: out[M, N] = epilogue(x[M, K] . w[N, K]^T) with M <= 64
+// (one row per sequence of a decode batch).  This is the reference's gemm_half /
+// gemm_half_residual small-M branch (kernels/gemm.cu:62-166) together with the RMSNorm,
+// ReLU^2 and tanh-cap passes around its decode call sites (src/model.cpp:110-177).
+//
+// At M <= 64 the work is streaming the weight: 2 bytes per weight element, 2*M flops.  The
+// kernel is laid out for that:
+//  * swap-AB: the weight tile is the MMA's A operand (M_mma = 128 output features per CTA) and
+//    the activations the B operand (N_mma = M rounded up to 16, 32 or 64), so one
+//    tcgen05.mma covers the whole batch and the accumulator is a 128 x N_mma fp32 tile in TMEM;
+//  * the weight is streamed by TMA in 128 x 64 (16 KB, 128-byte swizzled) boxes through a
+//    6-stage ring, marked L2 evict-first (read once per step; the activations, partials and
+//    KV caches stay in L2);
+//  * the K dimension is split across CTAs when N / 128 alone gives too few CTAs.  The S <= 8
+//    splits of one output tile are launched as one thread-block cluster: each CTA leaves its
+//    fp32 partial tile in its own shared memory, and after a cluster barrier CTA r sums rows
+//    m = r, r + S, ... of the tile over all S CTAs' shared memory (distributed shared memory
+//    loads, in split order, so results do not depend on timing) and runs the epilogue for
+//    them.  No global workspace, no atomics;
+//  * 6 stages of 16 + 2 KB leave room for two CTAs per SM, and the launch is a programmatic
+//    dependent launch: the weight boxes of the first stages are requested before
+//    griddepcontrol.wait (weights are never written by a preceding kernel), so a GEMM that
+//    follows another kernel starts streaming while that kernel finishes;
+//  * the epilogue applies the fused steps (RMSNorm row scale, residual, ReLU^2, tanh cap)
+//    on the fp32 sum and rounds once to bf16.
+//
+// Warp roles (192 threads): warp 0 lane 0 issues TMA, warp 1 issues the MMAs (elected lane)
+// and owns the TMEM allocation, warps 2-5 compute the RMSNorm scales, then read the
+// accumulator (warp w reads TMEM lanes 32*(w%4)..+31, the quarter its SM sub-partition may
+// access) and run the epilogue.  Every mbarrier wait is bounded (sm100_ptx.cuh).
+#include <cooperative_groups.h>
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/nanochat_attn.h"
+#include "nc_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace nc {
+
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kTileN = 128;                      // output features per CTA (MMA M)
+constexpr int kTileK = 64;                       // K per stage: one 128-byte swizzled row
+constexpr int kStages = 6;
+constexpr int kWBoxBytes = kTileN * kTileK * 2;  // 16 KB
+constexpr int kMaxRows = 64;
+constexpr int kMaxSplits = 8;                    // portable cluster size
+
+struct GemmTail {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t accum;
+    uint64_t drain;
+    float rnorm[kMaxRows];
+    uint32_t tmem;
+    int abort;
+};
+
+template <int MP>
+constexpr int gemm_smem_bytes() {
+    return kStages * (kWBoxBytes + MP * 128) + (int)sizeof(GemmTail) + 1024;
+}
+
+struct GemmParams {
+    bf16* out;
+    const bf16* x;
+    const bf16* residual;
+    int M, N, K;
+    int kb_total;       // ceil(K / 64)
+    int kb_per;         // K boxes per split
+    int splits;         // CTAs per output tile = cluster size along y
+    int flags;
+    float cap;
+    int seg_cols;
+    int* status;
+};
+
+// Wait tags (ORed with kStatusTimeoutMbar into the status word).
+constexpr int kTagEmpty = 0x41, kTagFull = 0x42, kTagAccum = 0x43, kTagDrainLoad = 0x44,
+              kTagDrainMma = 0x45;
+
+// Fused epilogue of one output element (row m, feature n) and its bf16 store.
+__device__ __forceinline__ void finish(const GemmParams& p, const float* rnorm, int m, int n,
+                                       float v) {
+    if (p.flags & NC_GEMM_NORM_INPUT) v *= rnorm[m];
+    if (p.flags & NC_GEMM_RESIDUAL) v += __bfloat162float(p.residual[(size_t)m * p.N + n]);
+    if (p.flags & NC_GEMM_RELU2) {
+        v = fmaxf(v, 0.f);
+        v *= v;
+    }
+    if (p.flags & NC_GEMM_TANH_CAP) v = p.cap * tanhf(v / p.cap);
+    const int seg = p.seg_cols;
+    p.out[(size_t)(n / seg) * ((size_t)p.M * seg) + (size_t)m * seg + (n % seg)] =
+        __float2bfloat16(v);
+}
+
+template <int MP>
+__global__ void __launch_bounds__(kGemmThreads, 2)
+    gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmX, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    // 128-byte swizzled TMA boxes want 1024-byte aligned destinations.
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sW = base;
+    uint8_t* sX = base + kStages * kWBoxBytes;
+    GemmTail* tail = reinterpret_cast<GemmTail*>(sX + kStages * MP * 128);
+    constexpr uint32_t kXBoxBytes = MP * 128;
+    constexpr uint32_t kTmemCols = MP < 32 ? 32 : MP;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    const int split = blockIdx.y;  // = rank in the cluster (cluster dims 1 x splits)
+    const int n0 = tile * kTileN;
+    const int kb0 = split * p.kb_per;
+    const int nkb = min(p.kb_total, kb0 + p.kb_per) - kb0;  // >= 1 (host plans no empty split)
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&tail->full[i], 1);
+            mbar_init(&tail->empty[i], 1);
+        }
+        mbar_init(&tail->accum, 1);
+        mbar_init(&tail->drain, 1);
+        tail->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmW);
+        prefetch_tmap(&tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tail->tmem, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem;
+    volatile int* abort_flag = &tail->abort;
+    // Let a dependent launch (the next GEMM of the step) start now: its CTAs take the SM slots
+    // this grid leaves free and stream their first weight boxes while this grid works; they
+    // read nothing this grid writes before their griddepcontrol.wait.
+    griddep_launch_dependents();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            const int pre = min(nkb, kStages);
+            // Weight boxes of the first stages: independent of earlier kernels.
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&tail->full[i], kWBoxBytes + kXBoxBytes);
+                tma_load_2d_hint(sW + i * kWBoxBytes, &tmW, &tail->full[i], (kb0 + i) * kTileK,
+                                 n0, pol);
+            }
+            griddep_wait();
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(sX + i * kXBoxBytes, &tmX, &tail->full[i], (kb0 + i) * kTileK, 0);
+            int issued = pre;
+            for (int i = pre; i < nkb; ++i) {
+                const int st = i % kStages;
+                if (!mbar_wait(&tail->empty[st], ((i / kStages) - 1) & 1, abort_flag, p.status,
+                               kTagEmpty))
+                    break;
+                mbar_arrive_expect_tx(&tail->full[st], kWBoxBytes + kXBoxBytes);
+                tma_load_2d_hint(sW + st * kWBoxBytes, &tmW, &tail->full[st],
+                                 (kb0 + i) * kTileK, n0, pol);
+                tma_load_2d(sX + st * kXBoxBytes, &tmX, &tail->full[st], (kb0 + i) * kTileK, 0);
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                // Leaving early: wait for the copies still in flight into this CTA's ring.
+                for (int i = max(issued - kStages, 0); i < issued; ++i)
+                    mbar_wait_drain(&tail->full[i % kStages], (i / kStages) & 1, p.status,
+                                    kTagDrainLoad);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        const uint32_t idesc = idesc_bf16_f32(kTileN, MP, false);  // both operands K-major
+        const uint64_t dW0 = smem_desc_sw128(smem_u32(sW), 16, 1024);
+        const uint64_t dX0 = smem_desc_sw128(smem_u32(sX), 16, 1024);
+        bool ok = true;
+        for (int i = 0; i < nkb; ++i) {
+            const int st = i % kStages;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tail->full[st], (i / kStages) & 1,
+                                                   abort_flag, p.status, kTagFull));
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t dW = dW0 + (uint64_t)(st * (kWBoxBytes >> 4));
+            const uint64_t dX = dX0 + (uint64_t)(st * (kXBoxBytes >> 4));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // 16 K-elements = 32 bytes per MMA
+                mma_ss_warp(tmem, dW + kk * 2, dX + kk * 2, idesc, (i | kk) ? 1u : 0u);
+            mma_commit_warp(&tail->empty[st]);
+        }
+        if (ok) {
+            mma_commit_warp(&tail->accum);
+        } else {
+            // Leaving early: wait for this warp's MMAs before TMEM is released.
+            mma_commit_warp(&tail->drain);
+            mbar_wait_drain(&tail->drain, 0, p.status, kTagDrainMma);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        const int n = n0 + quarter * 32 + lane;
+        griddep_wait();
+        if (p.flags & NC_GEMM_NORM_INPUT) {
+            // RMSNorm scale of each input row (reference kernels/rmsnorm.cu:17-48:
+            // rsqrt(sum(x^2) / n + 1e-6), fp32).
+            for (int m = warp - 2; m < p.M; m += 4) {
+                const bf16* row = p.x + (size_t)m * p.K;
+                float ss = 0.f;
+                for (int c = lane * 8; c < p.K; c += 256) {
+                    float f[8];
+                    bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss = __fmaf_rn(f[e], f[e], ss);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+                if (lane == 0) tail->rnorm[m] = rsqrtf(ss / (float)p.K + kNormEps);
+            }
+        }
+        float acc[MP];
+#pragma unroll
+        for (int m = 0; m < MP; ++m) acc[m] = 0.f;
+        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tail->accum, 0, abort_flag, p.status,
+                                                          kTagAccum));
+        tc_fence_after();
+        if (ok) {
+#pragma unroll
+            for (int c = 0; c < MP / 16; ++c) {
+                uint32_t r[16];
+                tmem_ld16_sync(tmem + ((uint32_t)(quarter * 32) << 16) + c * 16, r);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[c * 16 + j] = __uint_as_float(r[j]);
+            }
+        }
+        named_bar_sync(1, 128);  // RMSNorm scales visible to all epilogue threads
+        if (p.splits == 1) {
+            if (n < p.N) {
+#pragma unroll
+                for (int m = 0; m < MP; ++m)
+                    if (m < p.M) finish(p, tail->rnorm, m, n, acc[m]);
+            }
+        } else if (ok) {
+            // Partial tile into this CTA's (now idle) weight ring, [m][128] fp32.  Every copy
+            // into the ring has landed: each was consumed by an MMA that the accumulator
+            // barrier waited for.
+            float* red = reinterpret_cast<float*>(sW);
+            const int row = quarter * 32 + lane;  // the TMEM lane this thread read
+#pragma unroll
+            for (int m = 0; m < MP; ++m)
+                if (m < p.M) red[m * kTileN + row] = acc[m];
+        }
+    }
+
+    if (p.splits > 1) {
+        // Cluster reduction: all threads of all CTAs of the tile take both barriers.
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();  // release/acquire: every CTA's partial tile is visible
+        if (warp >= 2 && !*abort_flag) {
+            const int et = threadIdx.x - 64;
+            const int n = n0 + et;
+            const float* red = reinterpret_cast<const float*>(sW);
+            const float* parts[kMaxSplits];
+#pragma unroll
+            for (int r = 0; r < kMaxSplits; ++r)
+                parts[r] = r < p.splits ? cluster.map_shared_rank(red, r) : red;
+            if (n < p.N) {
+                for (int m = split; m < p.M; m += p.splits) {
+                    float v[kMaxSplits];
+#pragma unroll
+                    for (int r = 0; r < kMaxSplits; ++r)
+                        v[r] = r < p.splits ? parts[r][m * kTileN + et] : 0.f;
+                    float sum = v[0];
+#pragma unroll
+                    for (int r = 1; r < kMaxSplits; ++r)
+                        if (r < p.splits) sum += v[r];
+                    finish(p, tail->rnorm, m, n, sum);
+                }
+            }
+        }
+        cluster.sync();  // no CTA leaves while another still reads its shared memory
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// Row-major [rows][cols] bf16 matrix, box of 64 columns x box_rows rows, 128-byte swizzle;
+// rows and columns beyond the matrix read as zero.
+struct Map2DKey {
+    const void* base;
+    int rows, cols, box_rows, dev;
+    bool operator==(const Map2DKey& o) const {
+        return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+               dev == o.dev;
+    }
+};
+struct Map2DEntry {
+    Map2DKey key;
+    CUtensorMap map;
+    bool used;
+};
+std::mutex g_map2d_mutex;
+Map2DEntry g_map2d[512];
+
+bool map_2d(CUtensorMap* m, const void* base, int rows, int cols, int box_rows, int dev) {
+    const Map2DKey key{base, rows, cols, box_rows, dev};
+    size_t h = reinterpret_cast<uintptr_t>(base) >> 8;
+    h ^= (size_t)rows * 0x9E3779B1u ^ (size_t)cols * 0x85EBCA6Bu ^
+         (size_t)box_rows * 0xC2B2AE35u ^ (size_t)dev * 0x27D4EB2Fu;
+    h ^= h >> 13;
+    Map2DEntry& e = g_map2d[h & 511];
+    {
+        std::lock_guard<std::mutex> lk(g_map2d_mutex);
+        if (e.used && e.key == key) {
+            *m = e.map;
+            return true;
+        }
+    }
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTileK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    std::lock_guard<std::mutex> lk(g_map2d_mutex);
+    e.key = key;
+    e.map = *m;
+    e.used = true;
+    return true;
+}
+
+constexpr int kMaxDev = 64;
+
+struct GemmPlan {
+    int n_tiles, kb_total, kb_per, splits;
+};
+
+// Split count: aim for about two CTAs per SM of a B200 (148 SMs) over the whole grid, at most
+// kMaxSplits (one cluster per output tile); `req` > 0 sets it instead (clamped the same way).
+constexpr int kPlanSMs = 148;
+GemmPlan plan_gemm(int N, int K, int req) {
+    GemmPlan g;
+    g.n_tiles = (N + kTileN - 1) / kTileN;
+    g.kb_total = (K + kTileK - 1) / kTileK;
+    int s = req > 0 ? req : std::max(1, (2 * kPlanSMs) / g.n_tiles);
+    s = std::min(std::min(s, kMaxSplits), g.kb_total);
+    g.kb_per = (g.kb_total + s - 1) / s;
+    g.splits = (g.kb_total + g.kb_per - 1) / g.kb_per;  // no empty split
+    return g;
+}
+
+template <int MP>
+cudaError_t launch_mp(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& p,
+                      const GemmPlan& g, int dev, cudaStream_t stream) {
+    static bool attr_set[kMaxDev] = {};
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_skinny_kernel<MP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             gemm_smem_bytes<MP>());
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)g.n_tiles, (unsigned)g.splits);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = gemm_smem_bytes<MP>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = (unsigned)g.splits;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<MP>, mw, mx, p);
+}
+
+bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + bn && y < x + an;
+}
+
+}  // namespace
+
+}  // namespace nc
+
+extern "C" {
+
+int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual, int M, int N,
+                   int K, int flags, float cap, int seg_cols, int splits, cudaStream_t stream) {
+    using namespace nc;
+    if (M < 1 || M > kMaxRows || N < 1 || K < 8 || (K & 7) || splits < 0) return NC_ERR_INVALID_ARG;
+    if (flags & ~(NC_GEMM_NORM_INPUT | NC_GEMM_RESIDUAL | NC_GEMM_RELU2 | NC_GEMM_TANH_CAP))
+        return NC_ERR_INVALID_ARG;
+    if (!out || !x || !w || ((flags & NC_GEMM_RESIDUAL) && !residual)) return NC_ERR_INVALID_ARG;
+    if ((flags & NC_GEMM_TANH_CAP) && !(cap > 0.f)) return NC_ERR_INVALID_ARG;
+    if (seg_cols == 0) seg_cols = N;
+    if (seg_cols < 1 || N % seg_cols) return NC_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 1) || (reinterpret_cast<uintptr_t>(residual) & 1))
+        return NC_ERR_MISALIGNED;
+    if (overlaps(out, (size_t)M * N * 2, x, (size_t)M * K * 2)) return NC_ERR_INVALID_ARG;
+    if ((flags & NC_GEMM_RESIDUAL) && residual != out &&
+        overlaps(out, (size_t)M * N * 2, residual, (size_t)M * N * 2))
+        return NC_ERR_INVALID_ARG;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return internal_cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDev) return NC_ERR_INVALID_ARG;
+    int* status = nullptr;
+    int st = internal_status_word(&status);
+    if (st) return st;
+
+    const GemmPlan g = plan_gemm(N, K, splits);
+    const int mp = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    CUtensorMap mw, mx;
+    if (!map_2d(&mw, w, N, K, kTileN, dev) || !map_2d(&mx, x, M, K, mp, dev))
+        return NC_ERR_INVALID_ARG;
+    GemmParams p;
+    p.out = static_cast<bf16*>(out);
+    p.x = static_cast<const bf16*>(x);
+    p.residual = static_cast<const bf16*>(residual);
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.kb_total = g.kb_total;
+    p.kb_per = g.kb_per;
+    p.splits = g.splits;
+    p.flags = flags;
+    p.cap = cap;
+    p.seg_cols = seg_cols;
+    p.status = status;
+    if (mp == 16) e = launch_mp<16>(mw, mx, p, g, dev, stream);
+    else if (mp == 32) e = launch_mp<32>(mw, mx, p, g, dev, stream);
+    else e = launch_mp<64>(mw, mx, p, g, dev, stream);
+    return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
+}
+
+}  // extern "C"

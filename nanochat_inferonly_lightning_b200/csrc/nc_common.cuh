@@ -257,5 +257,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 // Both return an nc_status.
 int internal_rope_table(const float2** table);
 int internal_status_word(int** status);
+// Records `e` as this thread's last CUDA error and returns NC_ERR_CUDA.
+int internal_cuda_fail(cudaError_t e);
 
 }  // namespace nc

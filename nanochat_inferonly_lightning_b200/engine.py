@@ -12,8 +12,16 @@ What runs where:
   nc_rope_qknorm_append + nc_flash_attention per sequence (tcgen05 prefill); for each decode
   step, one nc_decode_attention over the whole batch (RoPE + QK-norm of q and k, append, and
   split-KV attention in one kernel), reading per-sequence lengths from a device array;
-* GEMMs on cuBLAS through torch (fp32 accumulation; product + residual rounded once), and the
-  parameter-free RMSNorm, ReLU^2, tanh cap and embedding gather as torch operations.
+* the decode step's GEMMs on this library's skinny tcgen05 GEMM (gemm.py, nc_gemm_skinny): one
+  pass over a fused [q; k; v] weight writing q, k and v separately, the output projection and
+  MLP down projection with the residual added in place, the MLP up projection with ReLU^2, and
+  the LM head with the tanh cap; the RMSNorm before the Q/K/V, MLP-up and LM-head GEMMs is a
+  per-row scale applied inside them.  A decode layer is four GEMM launches and one attention
+  launch;
+* the prompt pass's GEMMs (one sequence of P rows at a time) on cuBLAS through torch (fp32
+  accumulation; product + residual rounded once), the parameter-free RMSNorm, ReLU^2, tanh cap
+  and embedding gather as torch operations there, and the embedding gather + first RMSNorm and
+  the argmax of a decode step as torch operations.
 
 A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
 and replayed; the device length array advances inside the graph.  The reference engine runs one
@@ -25,6 +33,7 @@ import math
 import torch
 
 from . import attn
+from . import gemm as G
 
 N_LAYER = 34
 N_HEAD = 17
@@ -89,7 +98,14 @@ class BatchedEngine:
         self.ws = torch.zeros(attn.decode_workspace_bytes(batch, max_len, N_HEAD),
                               dtype=torch.uint8, device=device)
         self.tok = torch.zeros(batch, dtype=torch.int64, device=device)  # next input token
-        self.logits = None
+        # decode-step GEMM operands: fused [q; k; v] weights and the activations
+        self.wqkv = [torch.cat([l["q"], l["k"], l["v"]], 0) for l in weights.layers]
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.x = torch.zeros((batch, N_EMBD), **bf)           # residual stream
+        self.qkv = torch.zeros((3, batch, N_EMBD), **bf)      # q, k, v (pre-RoPE)
+        self.a = torch.zeros((batch, N_EMBD), **bf)           # attention output
+        self.h = torch.zeros((batch, MLP_HIDDEN), **bf)       # ReLU^2 of the MLP up projection
+        self.logits = torch.zeros((batch, VOCAB), **bf)
         self.graph = None
 
     # ------------------------------------------------------------------ prompt
@@ -120,19 +136,19 @@ class BatchedEngine:
     def _decode_body(self):
         """One greedy step for the whole batch: consumes self.tok, writes the next tokens back
         into self.tok.  Static shapes, device-side lengths: safe to capture."""
-        w = self.w
+        w, x, qkv, a, h = self.w, self.x, self.qkv, self.a, self.h
         self.kv_len.add_(1)  # the new token sits at row kv_len - 1
-        x = rmsnorm(w.embed[self.tok])
+        x.copy_(rmsnorm(w.embed[self.tok]))
         for i, l in enumerate(w.layers):
-            xn = rmsnorm(x)
-            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
-            a = torch.empty_like(q)
-            attn.decode_attention(a, q, k, v, self.k_tab[i], self.v_tab[i], self.kv_len, N_HEAD,
-                                  SCALE, self.max_len, self.ws)
-            x = torch.addmm(x, a, l["o"].t())
-            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
-            x = torch.addmm(x, h, l["down"].t())
-        self.logits = logits_of(w, x)  # [B, VOCAB] bf16, kept for inspection
+            # RMSNorm -> Q/K/V (src/model.cpp:110-116)
+            G.gemm_skinny(qkv, x, self.wqkv[i], flags=G.NORM_INPUT, seg_cols=N_EMBD)
+            attn.decode_attention(a, qkv[0], qkv[1], qkv[2], self.k_tab[i], self.v_tab[i],
+                                  self.kv_len, N_HEAD, SCALE, self.max_len, self.ws)
+            G.gemm_skinny(x, a, l["o"], residual=x)                      # :139
+            G.gemm_skinny(h, x, l["up"], flags=G.NORM_INPUT | G.RELU2)  # :146-150
+            G.gemm_skinny(x, h, l["down"], residual=x)                   # :153
+        # final RMSNorm, LM head, soft cap (:170-177); logits [B, VOCAB] kept for inspection
+        G.gemm_skinny(self.logits, x, w.lm_head, flags=G.NORM_INPUT | G.TANH_CAP, cap=LOGIT_CAP)
         self.tok.copy_(torch.argmax(self.logits.float(), dim=-1))
 
     def capture(self):

@@ -1,0 +1,51 @@
+"""Python mirror of the decode-step GEMM entry point (nc_gemm_skinny) over the C ABI.
+
+out[M, N] = epilogue(x[M, K] . w[N, K]^T) for M <= 64 rows, w in the reference layout W[out, in]
+(src/model.h:30-47), with the RMSNorm that precedes the reference's projections
+(kernels/rmsnorm.cu), the residual add of gemm_half_residual (kernels/gemm.cu:115-166), ReLU^2
+and the logit tanh cap (kernels/ops.cu:23-46) fused in as flags.  Tensors are torch CUDA bf16;
+the stream defaults to torch's current stream.  Raises NcError on a non-zero status.
+"""
+import ctypes
+
+from . import _lib
+from .attn import _bf16, _ptr, _stream
+
+NORM_INPUT = 1
+RESIDUAL = 2
+RELU2 = 4
+TANH_CAP = 8
+MAX_ROWS = 64
+
+
+def gemm_skinny(out, x, w, residual=None, flags=0, cap=0.0, seg_cols=0, splits=0, stream=None):
+    """out[M, N] (or N / seg_cols segments of [M, seg_cols]) = epilogue(x @ w.T).
+
+    flags: NORM_INPUT (scale row m of the product by rsqrt(mean(x[m]^2) + 1e-6)), RESIDUAL
+    (+ residual [M, N], which may be `out` itself), RELU2, TANH_CAP (cap * tanh(v / cap)),
+    applied in that order before one bf16 rounding.  splits: K-split count (0 = automatic,
+    at most 8)."""
+    _bf16(out, x, w, residual)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w is {tuple(w.shape)}, x is {tuple(x.shape)}")
+    if out.numel() != M * N:
+        raise ValueError(f"out has {out.numel()} elements, expected {M * N}")
+    if residual is not None:
+        flags |= RESIDUAL
+    lib = _lib.load()
+    _lib.check("nc_gemm_skinny",
+               lib.nc_gemm_skinny(_ptr(out), _ptr(x), _ptr(w), _ptr(residual), M, N, K, flags,
+                                  ctypes.c_float(cap), seg_cols, splits, _stream(stream)))
+    return out
+
+
+def gemm_half(C, A, B, M, N, K, stream=None):
+    """kernels/gemm.cu:62-113 for M <= 64: C[M, N] = A[M, K] @ B[N, K]^T."""
+    return gemm_skinny(C, A.view(M, K), B.view(N, K), stream=stream)
+
+
+def gemm_half_residual(D, A, B, residual, M, N, K, stream=None):
+    """kernels/gemm.cu:115-166 for M <= 64: D[M, N] = A[M, K] @ B[N, K]^T + residual[M, N]."""
+    return gemm_skinny(D, A.view(M, K), B.view(N, K), residual=residual, stream=stream)

@@ -114,15 +114,25 @@ def test_argument_validation_without_gpu():
         assert lib.nc_status_string(code) not in (b"", b"unknown status")
 
 
-def test_workspace_size_is_host_side_and_monotone():
+def test_gemm_argument_validation_without_gpu():
+    """nc_gemm_skinny rejects bad sizes, flags, segments, alignment and aliasing before any
+    CUDA call."""
     lib = _lib.load()
-    sizes = [lib.nc_decode_workspace_bytes(64, n, 17, 0) for n in (16, 256, 2048, 20480)]
-    assert all(s > 0 for s in sizes)
-    assert sizes == sorted(sizes)
-    assert lib.nc_decode_workspace_bytes(1, 512, 17, 16) >= 32 * 17 * 128 * 4
-    assert lib.nc_decode_workspace_bytes(0, 512, 17, 0) == 0
+    P = ctypes.c_void_p
+    F = ctypes.c_float
 
+    def call(out=0x10000, x=0x20000, w=0x40000, res=None, M=8, N=2176, K=2176, flags=0,
+             cap=0.0, seg=0, splits=0):
+        return lib.nc_gemm_skinny(P(out), P(x), P(w), None if res is None else P(res), M, N,
+                                  K, flags, F(cap), seg, splits, None)
 
-def test_python_mirror_raises_without_library(tmp_path):
-    with pytest.raises(RuntimeError, match="missing"):
-        _lib.load(str(tmp_path / "nope.so"))
+    assert call(M=0) == 1 and call(M=65) == 1          # 1 <= M <= 64
+    assert call(K=2180) == 1 and call(K=0) == 1         # K % 8 == 0, K >= 8
+    assert call(N=0) == 1 and call(splits=-1) == 1
+    assert call(flags=16) == 1                          # unknown flag
+    assert call(flags=2) == 1                           # residual flag without a residual
+    assert call(flags=8, cap=0.0) == 1                  # tanh cap needs cap > 0
+    assert call(seg=1000) == 1                          # segment must divide N
+    assert call(x=0x20008) == 2 and call(w=0x40004) == 2 and call(out=0x10001) == 2
+    assert call(out=0x20000 + 64) == 1                  # out overlaps x
+    assert call(res=0x10000 + 2, flags=2) == 1          # residual partly overlaps out

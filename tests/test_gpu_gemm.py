@@ -1,0 +1,226 @@
+"""Skinny tcgen05 GEMM of the decode step (nc_gemm_skinny) against a torch fp32 reference.
+
+The reference computes gemm_half in fp32 accumulation with one bf16 rounding
+(kernels/gemm.cu:62-113; gemm_half_residual adds the residual before that rounding,
+kernels/gemm.cu:115-166).  Checks: plain products over the batch sizes and shapes of the decode
+call sites (src/model.cpp:114-116, :139, :149-153, :174) plus ragged N and K tails; each fused
+step (RMSNorm row scale, residual, in-place residual, ReLU^2, tanh cap, segmented Q|K|V output);
+fixed-order split-K through a thread-block cluster (bit-identical repeats, CUDA-graph replay
+equal to eager, explicit split counts agreeing); and chains of dependent calls launched with
+programmatic dependent launch.
+
+Tolerance.  The tensor cores' fp32 accumulation is not exact fp32 summation: measured on B200
+against an fp64 product, cuBLAS's bf16 GEMM (torch.matmul) and this kernel without a K split
+give identical error statistics, up to 4.5e-4 x sum_k |x_k w_k| (and a K split only lowers the
+error).  So a result must be within one bf16 ulp of the fp64 product plus 1e-3 x that sum.
+"""
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+NORM_EPS = 1e-6
+
+
+@pytest.fixture(scope="module")
+def G():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import nanochat_inferonly_lightning_b200 as nc
+
+    yield nc.gemm
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) == 0, "a kernel's bounded wait gave up"
+
+
+def rnd(shape, seed, std=1.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(shape, generator=g, device="cuda") * std).to(torch.bfloat16)
+
+
+def ref_product(x, w):
+    return (x.double() @ w.double().t()).float()
+
+
+def accum_slack(x, w, scale=None):
+    """1e-3 x sum_k |x_k w_k| per output (times the row scale when the row is scaled)."""
+    mag = (x.double().abs() @ w.double().abs().t()).float() * 1e-3
+    return mag if scale is None else mag * scale
+
+
+def assert_ulp(got, want_f32, what, slack=0.0):
+    """got (bf16) against an fp32 result: within one bf16 ulp of it plus `slack`."""
+    want = want_f32.float()
+    d = (got.float() - want).abs()
+    bound = want.abs() * 2.0 ** -7 + 1e-6 + slack
+    bad = d > bound
+    assert not bad.any(), (f"{what}: {int(bad.sum())} of {d.numel()} beyond the bound, "
+                           f"max |d| {d.max().item():.3g}")
+
+
+@pytest.mark.parametrize("M", [1, 4, 8, 16, 17, 32, 33, 64])
+@pytest.mark.parametrize("N,K", [(2176, 2176), (8704, 2176), (2176, 8704)])
+def test_plain_product(G, M, N, K):
+    x, w = rnd((M, K), 1), rnd((N, K), 2, 0.02)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w)
+    torch.cuda.synchronize()
+    assert_ulp(out, ref_product(x, w), f"M={M} N={N} K={K}", accum_slack(x, w))
+
+
+@pytest.mark.parametrize("M,N,K", [(8, 200, 136), (3, 130, 72), (8, 65536, 2176),
+                                   (5, 6528, 2176), (2, 128, 8)])
+def test_ragged_and_large_shapes(G, M, N, K):
+    x, w = rnd((M, K), 3), rnd((N, K), 4, 0.05)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w)
+    torch.cuda.synchronize()
+    assert_ulp(out, ref_product(x, w), f"M={M} N={N} K={K}", accum_slack(x, w))
+
+
+@pytest.mark.parametrize("M", [1, 8, 40])
+def test_norm_input(G, M):
+    """NC_GEMM_NORM_INPUT: the product of RMSNorm(x) (kernels/rmsnorm.cu) with w.  Compared
+    with r_m * (x @ w^T) in fp32 (one ulp); the reference's own order, which rounds RMSNorm(x)
+    to bf16 before the GEMM, differs from that by the rounding of the normalised input, so it
+    gets the model tolerance (max 2e-2, mean 2e-3 absolute)."""
+    N, K = 8704, 2176
+    x, w = rnd((M, K), 7, 3.0), rnd((N, K), 8, 0.02)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w, flags=G.NORM_INPUT)
+    torch.cuda.synchronize()
+    xf = x.float()
+    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) / K + NORM_EPS)
+    assert_ulp(out, r * ref_product(x, w), f"norm M={M}", accum_slack(x, w, r))
+    # Reference order: RMSNorm(x) rounded to bf16 (relative error <= 2^-9 per element), then
+    # the GEMM: within one ulp, the accumulation slack and 2^-9 x sum_k |xn_k w_k|.
+    xn = (xf * r).to(torch.bfloat16)
+    want = ref_product(xn, w)
+    d = (out.float() - want).abs()
+    bound = want.abs() * 2.0 ** -7 + 1e-6 + accum_slack(x, w, r) * (1 + 2.0 ** -9 / 1e-3)
+    assert (d <= bound).all() and d.mean() <= 2e-3
+
+
+def test_residual_and_in_place(G):
+    M, N, K = 8, 2176, 8704
+    x, w, res = rnd((M, K), 9), rnd((N, K), 10, 0.02), rnd((M, N), 11)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w, residual=res)
+    acc = res.clone()
+    G.gemm_half_residual(acc, x, w, acc, M, N, K)  # in place, as src/model.cpp:139
+    torch.cuda.synchronize()
+    want = ref_product(x, w) + res.float()
+    assert_ulp(out, want, "residual", accum_slack(x, w))
+    assert torch.equal(acc, out)
+
+
+def test_relu2(G):
+    """NC_GEMM_RELU2 after NORM_INPUT: the MLP up projection (src/model.cpp:149-150)."""
+    M, N, K = 8, 8704, 2176
+    x, w = rnd((M, K), 12), rnd((N, K), 13, 0.02)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w, flags=G.NORM_INPUT | G.RELU2)
+    torch.cuda.synchronize()
+    xf = x.float()
+    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) / K + NORM_EPS)
+    # relu(v)^2 amplifies v's rounding by 2|v|: compare at two ulps of the squared value.
+    v = r * ref_product(x, w)
+    want = torch.relu(v).square()
+    d = (out.float() - want).abs()
+    assert (d <= want.abs() * 2.0 ** -6 + 1e-6 + 3 * v.abs() * accum_slack(x, w, r)).all()
+    assert int((out.float() == 0).sum()) > M * N // 3  # roughly half the products are < 0
+
+
+def test_tanh_cap_lm_head(G):
+    """NC_GEMM_NORM_INPUT | NC_GEMM_TANH_CAP: final norm, LM head and soft cap 15
+    (src/model.cpp:170-177) over the full 65536-row vocabulary."""
+    M, N, K, cap = 8, 65536, 2176, 15.0
+    x, w = rnd((M, K), 14), rnd((N, K), 15, 0.5)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w, flags=G.NORM_INPUT | G.TANH_CAP, cap=cap)
+    torch.cuda.synchronize()
+    xf = x.float()
+    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) / K + NORM_EPS)
+    want = cap * torch.tanh(r * ref_product(x, w) / cap)
+    assert want.abs().max() > 10.0  # the cap is exercised
+    d = (out.float() - want).abs()  # d tanh <= 1: the product's slack carries over
+    assert (d <= want.abs() * 2.0 ** -7 + 1e-4 + accum_slack(x, w, r)).all(), d.max()
+
+
+def test_segmented_qkv(G):
+    """A fused [q; k; v] weight with seg_cols = 2176 writes three [M, 2176] arrays: the three
+    projections of src/model.cpp:114-116 in one pass over the weights."""
+    M, D, K = 8, 2176, 2176
+    x = rnd((M, K), 16)
+    wq, wk, wv = rnd((D, K), 17, 0.02), rnd((D, K), 18, 0.02), rnd((D, K), 19, 0.02)
+    w = torch.cat([wq, wk, wv], 0)
+    out = torch.empty((3, M, D), dtype=torch.bfloat16, device="cuda")
+    G.gemm_skinny(out, x, w, flags=G.NORM_INPUT, seg_cols=D)
+    torch.cuda.synchronize()
+    xf = x.float()
+    r = torch.rsqrt(xf.square().sum(-1, keepdim=True) / K + NORM_EPS)
+    for i, wi in enumerate((wq, wk, wv)):
+        assert_ulp(out[i], r * ref_product(x, wi), f"segment {i}", accum_slack(x, wi, r))
+
+
+def test_split_k_deterministic_and_graph(G):
+    """Fixed-order split-K: repeats are bit-identical, a CUDA-graph replay equals the eager
+    call, and explicit split counts (1 to 8, and 136 clamped to 8) all meet the bound."""
+    M, N, K = 8, 2176, 8704
+    x, w, res = rnd((M, K), 20), rnd((N, K), 21, 0.02), rnd((M, N), 22)
+    outs = []
+    for _ in range(3):
+        o = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        G.gemm_skinny(o, x, w, residual=res)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    g_out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            G.gemm_skinny(g_out, x, w, residual=res)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(2):
+        g_out.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(g_out, outs[0])
+    want = ref_product(x, w) + res.float()
+    for splits in (1, 2, 3, 5, 7, 8, 136):
+        o = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        G.gemm_skinny(o, x, w, residual=res, splits=splits)
+        torch.cuda.synchronize()
+        assert_ulp(o, want, f"splits={splits}", accum_slack(x, w))
+    del graph
+
+
+def test_chain_of_dependent_calls(G):
+    """Back-to-back calls where each consumes the previous output (the decode step's
+    O -> up -> down chain, launched with programmatic dependent launch: each call streams
+    its first weight boxes before the previous one has finished) give the results of the same
+    calls separated by synchronizations."""
+    M, D, H = 8, 2176, 8704
+    x = rnd((M, D), 23)
+    a = rnd((M, D), 24)
+    wo, wu, wd = rnd((D, D), 25, 0.02), rnd((H, D), 26, 0.02), rnd((D, H), 27, 0.02)
+    xs = x.clone()
+    h = torch.empty((M, H), dtype=torch.bfloat16, device="cuda")
+    for _ in range(2):
+        G.gemm_skinny(xs, a, wo, residual=xs)
+        G.gemm_skinny(h, xs, wu, flags=G.NORM_INPUT | G.RELU2)
+        G.gemm_skinny(xs, h, wd, residual=xs)
+    torch.cuda.synchronize()
+    # same chain one call at a time with a synchronize between calls
+    xr = x.clone()
+    hr = torch.empty_like(h)
+    for _ in range(2):
+        G.gemm_skinny(xr, a, wo, residual=xr)
+        torch.cuda.synchronize()
+        G.gemm_skinny(hr, xr, wu, flags=G.NORM_INPUT | G.RELU2)
+        torch.cuda.synchronize()
+        G.gemm_skinny(xr, hr, wd, residual=xr)
+        torch.cuda.synchronize()
+    assert torch.equal(xs, xr) and torch.equal(h, hr)
