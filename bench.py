@@ -501,9 +501,12 @@ def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
 def bench_cfg5(dist):
     """cfg5: end-to-end greedy generation on the full 2.2B architecture with random N(0, 0.02)
     weights (seed 4), 8 sequences per GPU, 256-token prompts (uniform ids), 256 decode steps.
-    The attention path runs on this library (nanochat_inferonly_lightning_b200/engine.py);
-    GEMMs on cuBLAS, norms and elementwise ops on torch.  The prompt pass runs eagerly; each
-    decode step replays one CUDA graph for the whole batch.  Reported: decode tokens per
+    Each decode step replays one CUDA graph for the whole batch, all on this library
+    (nanochat_inferonly_lightning_b200/engine.py): per layer the fused Q/K/V GEMM (RMSNorm
+    fused), the decode attention (RoPE, QK-norm, append, split-KV), the output projection +
+    residual, the MLP up projection (RMSNorm, ReLU^2 fused) and down projection + residual on
+    the skinny tcgen05 GEMM, then the LM head (RMSNorm, tanh cap fused); the embedding gather
+    and argmax are torch operations.  The prompt pass runs eagerly with cuBLAS GEMMs.  Reported: decode tokens per
     second (whole job), timed with CUDA events over the 256 steps, and the prompt pass time."""
     from nanochat_inferonly_lightning_b200 import engine as E
 
@@ -540,8 +543,73 @@ def bench_cfg5(dist):
             "sequences_per_gpu": batch, "prompt_len": prompt_len, "decode_steps": steps,
             "timing": "CUDA events around 256 graph replays (whole batch per step); the "
                       "prompt pass (8 sequences, eager) is reported separately",
-            "note": "GEMMs are cuBLAS and the norms/elementwise ops torch: the step is "
-                    "bound by streaming the 4.4 GB of weights, not by attention"}
+            "note": "decode step: skinny tcgen05 GEMMs with fused RMSNorm/residual/ReLU^2/"
+                    "tanh cap and this library's decode attention; bound by streaming the "
+                    "4.15 GB of weights read per step"}
+
+
+GEMM_SHAPES = (  # decode-step GEMMs of the full architecture (src/model.cpp:110-177)
+    ("qkv", 3 * 2176, 2176, "NORM_INPUT", 2176),
+    ("o", 2176, 2176, "RESIDUAL", 0),
+    ("up", 8704, 2176, "NORM_INPUT|RELU2", 0),
+    ("down", 2176, 8704, "RESIDUAL", 0),
+    ("lm_head", 65536, 2176, "NORM_INPUT|TANH_CAP", 0),
+)
+
+
+def bench_gemm(dist, stepper, K, Wm, peaks, traffic, M=8):
+    """The skinny tcgen05 GEMM on each decode-step shape at M = 8 rows (the cfg5 batch), with
+    its fused epilogue.  A step calls it once per copy of the weight, over enough copies
+    (> 2x L2 together) that every call streams its weight from HBM, as in the engine where each
+    layer's weights are read once per step.  Calls run back to back from a CUDA graph
+    (programmatic dependent launch lets each start streaming while the previous one finishes).  Algorithmic bytes per
+    call: the weight N*K*2 plus x, the output and the residual."""
+    import nanochat_inferonly_lightning_b200 as nc
+
+    G = nc.gemm
+    out = {}
+    for name, N, Kd, flag_names, seg in GEMM_SHAPES:
+        flags = 0
+        for f in flag_names.split("|"):
+            flags |= getattr(G, f)
+        copies = max(2, -(-int(2.2 * L2_BYTES) // (N * Kd * 2)))
+        g = torch.Generator(device="cuda").manual_seed(40 + dist.rank)
+        ws = [(torch.randn((N, Kd), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+              for _ in range(copies)]
+        x = torch.randn((M, Kd), generator=g, device="cuda").to(torch.bfloat16)
+        res = torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        kw = dict(flags=flags & ~G.RESIDUAL, cap=15.0, seg_cols=seg)
+        if flags & G.RESIDUAL:
+            kw["residual"] = res
+
+        def calls():
+            for wt in ws:
+                G.gemm_skinny(y, x, wt, **kw)
+
+        # One step = one replay of a CUDA graph of the calls (as the engine replays its decode
+        # step), so the host's per-call cost is not in the timed region.
+        calls()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                calls()
+        torch.cuda.current_stream().wait_stream(side)
+        t_ms = stepper.run(graph.replay, K, Wm) / copies
+        del graph
+        nbytes = N * Kd * 2 + M * Kd * 2 + M * N * 2 * (2 if flags & G.RESIDUAL else 1)
+        gbs = nbytes / (t_ms * 1e-3) / 1e9
+        out[name] = {"N": N, "K": Kd, "M": M, "fused": flag_names, "us": t_ms * 1e3,
+                     "GB_per_s": gbs, "frac_hbm": gbs / peaks["hbm"],
+                     "traffic": traffic.get(f"gemm_skinny_{name}_m8")}
+        del ws
+        torch.cuda.empty_cache()
+    out["peak_src"] = peaks["src"]
+    out["timing"] = ("mean per call: K replays of a CUDA graph of one call per weight copy, back "
+                     "to back between two CUDA events; weight copies > 2x L2 together")
+    return out
 
 
 def bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic):
@@ -633,7 +701,8 @@ def main():
     ap.add_argument("--impl", choices=["nc", "reference"], default="nc")
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
-    ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4"], default=None,
+    ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4", "gemm", "cfg5"],
+                    default=None,
                     help="run one workload only (profiling); implies --no-cpu, no e2e")
     args = ap.parse_args()
     K, Wm = args.steps, max(args.warmup, 3)
@@ -657,7 +726,9 @@ def main():
                                            [W.CFG1_LEN], "cfg1"),
               "cfg3": lambda: bench_decode(impl, dist, stepper, K, Wm, peaks, traffic,
                                            W.cfg3_kv_lens(), "cfg3"),
-              "cfg4": lambda: bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic)}[args.only]
+              "cfg4": lambda: bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic),
+              "gemm": lambda: bench_gemm(dist, stepper, K, Wm, peaks, traffic),
+              "cfg5": lambda: bench_cfg5(dist)}[args.only]
         r = fn()
         if dist.rank == 0:
             print(json.dumps({"only": args.only, "impl": args.impl, **r}), flush=True)
@@ -675,6 +746,7 @@ def main():
                                             W.cfg3_kv_lens(), "cfg3")
         extra["cfg4_chunked_prefill"] = bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic)
         if impl.kind == "nc":
+            extra["decode_step_gemms"] = bench_gemm(dist, stepper, K, Wm, peaks, traffic)
             extra["cfg5_e2e_generation"] = bench_cfg5(dist)
     clk = clocks.stop()
 

@@ -105,6 +105,19 @@ int nc_decode_attention(void* out, const void* q, const void* k_new, const void*
                         int batch, int heads, float scale, int max_kv_len, int split_len,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* nc_decode_attention for a call that directly follows, on the same stream, a kernel that
+ * writes none of the caches, kv_len or the two pointer arrays (typically the Q/K/V projection
+ * of nc_gemm_skinny).  Small batches (the per-head layout) then launch as a programmatic
+ * dependent launch: the call's CTAs start while that kernel is still running and load their
+ * cache rows, lengths and cache bases before waiting for it; q, k_new, v_new and every write
+ * come after the wait.  Results are those of nc_decode_attention.  Not for a call right after
+ * a kernel that appends to the same caches (nc_rope_qknorm_append, another decode call): its
+ * rows could be read before they are written.  No counterpart in the reference. */
+int nc_decode_attention_overlap(void* out, const void* q, const void* k_new, const void* v_new,
+                                void* const* k_caches, void* const* v_caches, const int* kv_len,
+                                int batch, int heads, float scale, int max_kv_len, int split_len,
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* nc_decode_attention without the workspace argument, for callers that cannot allocate
  * device memory (an engine whose device memory is planned by an outside allocator, a host
  * binding with no device allocator to pass a workspace, or a latency-critical loop where
@@ -180,7 +193,7 @@ int nc_kv_cache_decode(nc_kv_cache* cache, int layer, void* out, const void* q,
  * Skinny GEMM for the decode step: out[M, N] = epilogue(x[M, K] . w[N, K]^T) for 1 <= M <= 64
  * rows (one per sequence of a decode batch), bf16 operands, fp32 accumulation on the tcgen05
  * tensor cores, one bf16 rounding of the result.  w is a weight in the reference layout
- * W[out, in] and is streamed from HBM once; the K dimension is split across up to 8 CTAs of one
+ * W[out, in] and is streamed from HBM once; the K dimension is split across up to 12 CTAs of one
  * thread-block cluster when N alone gives too few tiles (partials are summed through
  * distributed shared memory in a fixed order: results are deterministic, no workspace).
  * Optional steps, chosen by `flags`, are fused so that each replaces a separate pass:
@@ -194,7 +207,7 @@ int nc_kv_cache_decode(nc_kv_cache* cache, int layer, void* out, const void* q,
  * N / seg_cols segments stored one after another, each [M, seg_cols]: a fused Q|K|V weight
  * then writes q, k and v as three separate [M, 2176] arrays.
  * Requirements: K % 8 == 0; x and w 16-byte aligned; out must not overlap x; `splits` 0 picks
- * the split count, else that many (clamped to [1, 8] and to the number of 64-wide K blocks).
+ * the split count, else that many (clamped to [1, 12] and to the number of 64-wide K blocks).
  * Replaces: gemm_half / gemm_half_residual for M <= 16 (kernels/gemm.cu:62-166, the small-M
  * branch) at the decode call sites src/model.cpp:114-116, :139, :149-150, :153, :174-177,
  * together with the rmsnorm / relu_squared / tanh_cap launches around them. */

@@ -88,21 +88,24 @@ def decode_workspace_bytes(batch, max_kv_len, heads, split_len=0):
 
 
 def decode_attention(out, q, k_new, v_new, k_ptrs, v_ptrs, kv_len, heads, scale, max_kv_len,
-                     workspace, split_len=0, stream=None):
+                     workspace, split_len=0, stream=None, overlap=False):
     """Batched decode step (include/nanochat_attn.h nc_decode_attention).
 
     k_ptrs/v_ptrs: int64 CUDA tensors [B] of per-sequence cache base addresses; kv_len: int32
     CUDA tensor [B]; workspace: a zero-filled uint8 CUDA tensor of at least
-    decode_workspace_bytes(B, max_kv_len, heads, split_len) bytes."""
+    decode_workspace_bytes(B, max_kv_len, heads, split_len) bytes.  overlap=True calls
+    nc_decode_attention_overlap: only right after a kernel that writes none of the caches,
+    kv_len or the pointer arrays (e.g. the Q/K/V projection)."""
     _bf16(out, q, k_new, v_new)
     batch = int(kv_len.numel())
     lib = _lib.load()
-    _lib.check("nc_decode_attention",
-               lib.nc_decode_attention(_ptr(out), _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(k_ptrs),
-                                       _ptr(v_ptrs), _ptr(kv_len), batch, heads, float(scale),
-                                       max_kv_len, split_len, _ptr(workspace),
-                                       workspace.numel() if workspace is not None else 0,
-                                       _stream(stream)))
+    name = "nc_decode_attention_overlap" if overlap else "nc_decode_attention"
+    _lib.check(name,
+               getattr(lib, name)(_ptr(out), _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(k_ptrs),
+                                  _ptr(v_ptrs), _ptr(kv_len), batch, heads, float(scale),
+                                  max_kv_len, split_len, _ptr(workspace),
+                                  workspace.numel() if workspace is not None else 0,
+                                  _stream(stream)))
 
 
 def prefill_attention_batched(out, q, k_slab, v_slab, seq_stride, rows_per_seq, kv_offset,

@@ -146,7 +146,7 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
                   void* const* k_caches, void* const* v_caches, void* k_single, void* v_single,
                   const int* kv_len, int n_visible_single, int batch, int heads, float scale,
                   int max_kv_len, int split_len, void* ws, size_t ws_bytes,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, int overlap = 0) {
     // The decode kernel runs one warp per head plus a producer warp (<= 1024 threads).
     if (batch < 0 || heads < 1 || heads > 31 || max_kv_len < 0) return NC_ERR_INVALID_ARG;
     if (batch == 0) return NC_OK;
@@ -182,6 +182,7 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
     a.heads = heads;
     a.q_raw = k_new != nullptr;
     a.head_layout = decode_use_head_layout(batch, max_kv_len, split_len) ? 1 : 0;
+    a.overlap = overlap && a.head_layout ? 1 : 0;
     a.scale_log2 = scale * kLog2e;
     a.split_len = T;
     a.max_splits = max_splits;
@@ -373,6 +374,16 @@ int nc_decode_attention(void* out, const void* q, const void* k_new, const void*
     return decode_common(out, q, k_new, v_new, k_caches, v_caches, nullptr, nullptr, kv_len, 0,
                          batch, heads, scale, max_kv_len, split_len, workspace,
                          workspace_bytes, stream);
+}
+
+int nc_decode_attention_overlap(void* out, const void* q, const void* k_new, const void* v_new,
+                                void* const* k_caches, void* const* v_caches, const int* kv_len,
+                                int batch, int heads, float scale, int max_kv_len, int split_len,
+                                void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (batch > 0 && (!k_caches || !v_caches || !kv_len)) return NC_ERR_INVALID_ARG;
+    return decode_common(out, q, k_new, v_new, k_caches, v_caches, nullptr, nullptr, kv_len, 0,
+                         batch, heads, scale, max_kv_len, split_len, workspace,
+                         workspace_bytes, stream, 1);
 }
 
 int nc_prefill_attention_batched(void* out, const void* q, const void* k_slab,

@@ -473,12 +473,12 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     const int H = a.heads;
     const size_t rowstride = (size_t)H * kHeadDim;
     const size_t qoff = (size_t)b * rowstride + (size_t)h * kHeadDim + 8 * sub;
-    // Independent loads first, so that they share one round trip: the sequence's length, its
-    // cache bases and this head's query.
+    // The sequence's length and cache bases first, then this split's cache rows: none of them
+    // is written by the kernel that precedes an overlapped launch (a.overlap), so they are
+    // read before griddepcontrol.wait; the query and the new key and value come after it.
     const int Lraw = raw_len(a, b);
     bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
     bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
-    const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
     const int L = min(Lraw, a.max_kv_len);
     const int T = a.split_len;
     const int n_splits = L > 0 ? (L + T - 1) / T : 1;
@@ -487,6 +487,7 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
         atomicOr(a.status, kStatusDecodeBound);
     bf16* out_row = a.out + (size_t)b * rowstride + (size_t)h * kHeadDim;
     if (L <= 0) {
+        griddep_wait();
         // No visible key: the reference's 0/0 yields NaN (flash_attention.cu:155).
         if (warp == 0 && half == 0)
             *reinterpret_cast<uint4*>(out_row + 8 * sub) =
@@ -513,6 +514,8 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
             kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
         }
     }
+    griddep_wait();  // no-op unless launched as a programmatic dependent launch
+    const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
     float qf[8];
     {
         if (a.q_raw) {
@@ -783,9 +786,16 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         attr[dev] = true;
     }
     if (a.head_layout) {
-        decode_head_kernel<<<dim3((unsigned)a.max_splits, (unsigned)a.heads, (unsigned)a.batch),
-                             128, 0, stream>>>(a);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)a.max_splits, (unsigned)a.heads, (unsigned)a.batch);
+        cfg.blockDim = dim3(128);
+        cfg.stream = stream;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = a.overlap ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, decode_head_kernel, a);
     }
     const long long items = (long long)a.max_splits * a.batch;
     const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(items, sms[dev]));

@@ -142,8 +142,11 @@ class BatchedEngine:
         for i, l in enumerate(w.layers):
             # RMSNorm -> Q/K/V (src/model.cpp:110-116)
             G.gemm_skinny(qkv, x, self.wqkv[i], flags=G.NORM_INPUT, seg_cols=N_EMBD)
+            # right after the Q/K/V GEMM, which writes no cache: the attention CTAs may start
+            # loading cache rows while it finishes
             attn.decode_attention(a, qkv[0], qkv[1], qkv[2], self.k_tab[i], self.v_tab[i],
-                                  self.kv_len, N_HEAD, SCALE, self.max_len, self.ws)
+                                  self.kv_len, N_HEAD, SCALE, self.max_len, self.ws,
+                                  overlap=True)
             G.gemm_skinny(x, a, l["o"], residual=x)                      # :139
             G.gemm_skinny(h, x, l["up"], flags=G.NORM_INPUT | G.RELU2)  # :146-150
             G.gemm_skinny(x, h, l["down"], residual=x)                   # :153

@@ -24,7 +24,7 @@ def gemm_skinny(out, x, w, residual=None, flags=0, cap=0.0, seg_cols=0, splits=0
     flags: NORM_INPUT (scale row m of the product by rsqrt(mean(x[m]^2) + 1e-6)), RESIDUAL
     (+ residual [M, N], which may be `out` itself), RELU2, TANH_CAP (cap * tanh(v / cap)),
     applied in that order before one bf16 rounding.  splits: K-split count (0 = automatic,
-    at most 8)."""
+    at most 12)."""
     _bf16(out, x, w, residual)
     M, K = x.shape
     N = w.shape[0]

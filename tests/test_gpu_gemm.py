@@ -165,7 +165,7 @@ def test_segmented_qkv(G):
 
 def test_split_k_deterministic_and_graph(G):
     """Fixed-order split-K: repeats are bit-identical, a CUDA-graph replay equals the eager
-    call, and explicit split counts (1 to 8, and 136 clamped to 8) all meet the bound."""
+    call, and explicit split counts (1 to 12, 16 and 136 clamped to 12) all meet the bound."""
     M, N, K = 8, 2176, 8704
     x, w, res = rnd((M, K), 20), rnd((N, K), 21, 0.02), rnd((M, N), 22)
     outs = []
@@ -189,7 +189,7 @@ def test_split_k_deterministic_and_graph(G):
     torch.cuda.synchronize()
     assert torch.equal(g_out, outs[0])
     want = ref_product(x, w) + res.float()
-    for splits in (1, 2, 3, 5, 7, 8, 136):
+    for splits in (1, 2, 3, 5, 7, 8, 12, 16, 136):
         o = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
         G.gemm_skinny(o, x, w, residual=res, splits=splits)
         torch.cuda.synchronize()

@@ -290,6 +290,47 @@ def test_decode_batched_streaming_layout(nc):
     _decode_batch(nc, [1, 5, 16, 33, 64, 128, 300, 511, 777, 1024, 1500, 2047], 0, seed=450)
 
 
+def test_decode_overlap_after_qkv_gemm(nc):
+    """nc_decode_attention_overlap right after the fused Q/K/V GEMM that produces its q, k_new
+    and v_new (the engine's order): the attention CTAs load cache rows while the GEMM runs and
+    wait for it before reading q/k/v.  Same bits as the plain call made after a synchronize, and
+    the oracle's result for the GEMM's q/k/v.  Eight sequences of up to 520 keys: the per-head
+    layout."""
+    lens = [257, 300, 333, 401, 450, 479, 505, 520]
+    B, max_len = len(lens), 520
+    g = torch.Generator(device="cuda").manual_seed(610)
+    x = torch.randn((B, H * D), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((3 * H * D, H * D), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    kcs = [normed(randn_u16((max_len, H, D), 620 + b), 0) for b in range(B)]
+    vcs = [randn_u16((max_len, H, D), 640 + b) for b in range(B)]
+    lt = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    results = []
+    for overlap in (True, False):
+        tk, tv = [dev(k) for k in kcs], [dev(v) for v in vcs]
+        kp = torch.tensor([t.data_ptr() for t in tk], dtype=torch.int64, device="cuda")
+        vp = torch.tensor([t.data_ptr() for t in tv], dtype=torch.int64, device="cuda")
+        ws = torch.zeros(nc.decode_workspace_bytes(B, max_len, H), dtype=torch.uint8,
+                         device="cuda")
+        qkv = torch.empty((3, B, H * D), dtype=torch.bfloat16, device="cuda")
+        out = torch.empty((B, H * D), dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        nc.gemm.gemm_skinny(qkv, x, w, flags=nc.gemm.NORM_INPUT, seg_cols=H * D)
+        if not overlap:
+            torch.cuda.synchronize()
+        nc.decode_attention(out, qkv[0], qkv[1], qkv[2], kp, vp, lt, H, SCALE, max_len, ws,
+                            overlap=overlap)
+        torch.cuda.synchronize()
+        results.append((bf16_to_u16(out), [bf16_to_u16(t) for t in tk],
+                        [bf16_to_u16(t) for t in tv], bf16_to_u16(qkv)))
+    (o1, k1, v1, qkv1), (o2, k2, v2, qkv2) = results
+    assert np.array_equal(qkv1, qkv2) and np.array_equal(o1, o2)
+    assert all(np.array_equal(a, b) for a, b in zip(k1, k2))
+    assert all(np.array_equal(a, b) for a, b in zip(v1, v2))
+    qkv1 = qkv1.reshape(3, B, H, D)
+    want, _, _ = oracle.decode_step(qkv1[0], qkv1[1], qkv1[2], kcs, vcs, lens, H, SCALE)
+    assert_close_bf16(o1.reshape(B, H * D), want, what="overlapped decode")
+
+
 def test_decode_cfg3_lengths_subset(nc):
     """First 8 sequences of cfg3's kv_len draw (torch seed 2)."""
     from nanochat_inferonly_lightning_b200 import workloads
