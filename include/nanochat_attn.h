@@ -220,6 +220,22 @@ enum {
 int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual, int M, int N,
                    int K, int flags, float cap, int seg_cols, int splits, cudaStream_t stream);
 
+/* ----------------------------------------------------------------------------------------
+ * The two ends of a decode step.
+ * out[r, :] = RMSNorm(table[tokens[r], :]) (eps 1e-6, one bf16 rounding): the embedding gather
+ * and the RMSNorm after it in one pass.  dim % 8 == 0, dim <= 8192; out and table 16-byte
+ * aligned.  A token id outside [0, vocab) gives a zero row and sets bit 0x800 of the device
+ * status word (nc_device_status).
+ * Replaces: embedding (kernels/ops.cu:9-20) + rmsnorm (kernels/rmsnorm.cu:9-63), called at
+ * src/model.cpp:158-162. */
+int nc_embed_rmsnorm(void* out, const void* table, const int* tokens, int rows, int dim,
+                     int vocab, cudaStream_t stream);
+/* out[r] = index of the first maximum of logits[r, :] (bf16 [rows, cols], cols % 8 == 0,
+ * 16-byte aligned), on the device.
+ * Replaces: the greedy branch of Engine::sample (src/engine.cpp:88-95) and the device-to-host
+ * copy of the logits before it. */
+int nc_argmax_rows(int* out, const void* logits, int rows, int cols, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

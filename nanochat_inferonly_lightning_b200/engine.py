@@ -17,11 +17,11 @@ What runs where:
   MLP down projection with the residual added in place, the MLP up projection with ReLU^2, and
   the LM head with the tanh cap; the RMSNorm before the Q/K/V, MLP-up and LM-head GEMMs is a
   per-row scale applied inside them.  A decode layer is four GEMM launches and one attention
-  launch;
+  launch; the step starts with one embedding-gather + RMSNorm launch and ends with an argmax
+  launch on the device (gemm.py);
 * the prompt pass's GEMMs (one sequence of P rows at a time) on cuBLAS through torch (fp32
-  accumulation; product + residual rounded once), the parameter-free RMSNorm, ReLU^2, tanh cap
-  and embedding gather as torch operations there, and the embedding gather + first RMSNorm and
-  the argmax of a decode step as torch operations.
+  accumulation; product + residual rounded once), with the parameter-free RMSNorm, ReLU^2, tanh
+  cap and embedding gather as torch operations there.
 
 A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
 and replayed; the device length array advances inside the graph.  The reference engine runs one
@@ -97,7 +97,7 @@ class BatchedEngine:
         self.kv_len = torch.zeros(batch, dtype=torch.int32, device=device)
         self.ws = torch.zeros(attn.decode_workspace_bytes(batch, max_len, N_HEAD),
                               dtype=torch.uint8, device=device)
-        self.tok = torch.zeros(batch, dtype=torch.int64, device=device)  # next input token
+        self.tok = torch.zeros(batch, dtype=torch.int32, device=device)  # next input token
         # decode-step GEMM operands: fused [q; k; v] weights and the activations
         self.wqkv = [torch.cat([l["q"], l["k"], l["v"]], 0) for l in weights.layers]
         bf = dict(dtype=torch.bfloat16, device=device)
@@ -138,7 +138,7 @@ class BatchedEngine:
         into self.tok.  Static shapes, device-side lengths: safe to capture."""
         w, x, qkv, a, h = self.w, self.x, self.qkv, self.a, self.h
         self.kv_len.add_(1)  # the new token sits at row kv_len - 1
-        x.copy_(rmsnorm(w.embed[self.tok]))
+        G.embed_rmsnorm(x, w.embed, self.tok)  # embedding + RMSNorm (:158-162)
         for i, l in enumerate(w.layers):
             # RMSNorm -> Q/K/V (src/model.cpp:110-116)
             G.gemm_skinny(qkv, x, self.wqkv[i], flags=G.NORM_INPUT, seg_cols=N_EMBD)
@@ -152,7 +152,7 @@ class BatchedEngine:
             G.gemm_skinny(x, h, l["down"], residual=x)                   # :153
         # final RMSNorm, LM head, soft cap (:170-177); logits [B, VOCAB] kept for inspection
         G.gemm_skinny(self.logits, x, w.lm_head, flags=G.NORM_INPUT | G.TANH_CAP, cap=LOGIT_CAP)
-        self.tok.copy_(torch.argmax(self.logits.float(), dim=-1))
+        G.argmax_rows(self.tok, self.logits)  # greedy choice (src/engine.cpp:88-95)
 
     def capture(self):
         """Capture one decode step in a CUDA graph (after one eager warm-up step, which also

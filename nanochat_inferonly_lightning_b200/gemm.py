@@ -5,8 +5,12 @@ out[M, N] = epilogue(x[M, K] . w[N, K]^T) for M <= 64 rows, w in the reference l
 (kernels/rmsnorm.cu), the residual add of gemm_half_residual (kernels/gemm.cu:115-166), ReLU^2
 and the logit tanh cap (kernels/ops.cu:23-46) fused in as flags.  Tensors are torch CUDA bf16;
 the stream defaults to torch's current stream.  Raises NcError on a non-zero status.
+Also here: the two small passes at the ends of a decode step (embedding gather + RMSNorm, and
+greedy argmax on the device).
 """
 import ctypes
+
+import torch
 
 from . import _lib
 from .attn import _bf16, _ptr, _stream
@@ -49,3 +53,30 @@ def gemm_half(C, A, B, M, N, K, stream=None):
 def gemm_half_residual(D, A, B, residual, M, N, K, stream=None):
     """kernels/gemm.cu:115-166 for M <= 64: D[M, N] = A[M, K] @ B[N, K]^T + residual[M, N]."""
     return gemm_skinny(D, A.view(M, K), B.view(N, K), residual=residual, stream=stream)
+
+
+def embed_rmsnorm(out, table, tokens, stream=None):
+    """kernels/ops.cu:9-20 + kernels/rmsnorm.cu:9-63 in one pass: out[r] = RMSNorm(table[tokens[r]]).
+    tokens: int32 CUDA tensor [rows]; table [vocab, dim]; out [rows, dim]."""
+    _bf16(out, table)
+    if tokens.dtype != torch.int32:
+        raise TypeError(f"tokens must be int32, got {tokens.dtype}")
+    rows, dim = int(tokens.numel()), int(table.shape[1])
+    lib = _lib.load()
+    _lib.check("nc_embed_rmsnorm",
+               lib.nc_embed_rmsnorm(_ptr(out), _ptr(table), _ptr(tokens), rows, dim,
+                                    int(table.shape[0]), _stream(stream)))
+    return out
+
+
+def argmax_rows(out, logits, stream=None):
+    """Greedy sampling of src/engine.cpp:88-95 on the device: out[r] (int32) = index of the
+    first maximum of logits[r] (bf16 [rows, cols])."""
+    _bf16(logits)
+    if out.dtype != torch.int32:
+        raise TypeError(f"out must be int32, got {out.dtype}")
+    rows, cols = logits.shape
+    lib = _lib.load()
+    _lib.check("nc_argmax_rows",
+               lib.nc_argmax_rows(_ptr(out), _ptr(logits), rows, cols, _stream(stream)))
+    return out

@@ -136,3 +136,16 @@ def test_gemm_argument_validation_without_gpu():
     assert call(x=0x20008) == 2 and call(w=0x40004) == 2 and call(out=0x10001) == 2
     assert call(out=0x20000 + 64) == 1                  # out overlaps x
     assert call(res=0x10000 + 2, flags=2) == 1          # residual partly overlaps out
+
+
+def test_step_ops_argument_validation_without_gpu():
+    lib = _lib.load()
+    P = ctypes.c_void_p
+    assert lib.nc_embed_rmsnorm(P(256), P(256), P(256), 4, 2180, 100, None) == 1  # dim % 8
+    assert lib.nc_embed_rmsnorm(P(256), P(256), P(256), 4, 16384, 100, None) == 1  # dim > 8192
+    assert lib.nc_embed_rmsnorm(P(256), P(256), P(256), 4, 2176, 0, None) == 1    # vocab
+    assert lib.nc_embed_rmsnorm(P(264), P(256), P(256), 4, 2176, 100, None) == 2  # alignment
+    assert lib.nc_embed_rmsnorm(P(256), P(256), P(256), 0, 2176, 100, None) == 0  # empty
+    assert lib.nc_argmax_rows(P(256), P(256), 4, 65530, None) == 1                 # cols % 8
+    assert lib.nc_argmax_rows(P(256), P(264), 4, 65536, None) == 2
+    assert lib.nc_argmax_rows(P(256), P(256), 0, 65536, None) == 0

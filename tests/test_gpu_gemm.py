@@ -7,7 +7,8 @@ call sites (src/model.cpp:114-116, :139, :149-153, :174) plus ragged N and K tai
 step (RMSNorm row scale, residual, in-place residual, ReLU^2, tanh cap, segmented Q|K|V output);
 fixed-order split-K through a thread-block cluster (bit-identical repeats, CUDA-graph replay
 equal to eager, explicit split counts agreeing); and chains of dependent calls launched with
-programmatic dependent launch.
+programmatic dependent launch.  Also the two passes at the ends of a decode step: the embedding
+gather + RMSNorm and the on-device first-maximum argmax.
 
 Tolerance.  The tensor cores' fp32 accumulation is not exact fp32 summation: measured on B200
 against an fp64 product, cuBLAS's bf16 GEMM (torch.matmul) and this kernel without a K split
@@ -224,3 +225,54 @@ def test_chain_of_dependent_calls(G):
         G.gemm_skinny(xr, hr, wd, residual=xr)
         torch.cuda.synchronize()
     assert torch.equal(xs, xr) and torch.equal(h, hr)
+
+
+# ----------------------------------------------------------------------- ends of a decode step
+def test_embed_rmsnorm(G):
+    """nc_embed_rmsnorm against the reference's two passes (kernels/ops.cu:9-20 gather, then
+    kernels/rmsnorm.cu: x * rsqrt(sum(x^2)/n + 1e-6), one bf16 rounding) computed in fp64:
+    within one bf16 ulp.  Repeated and out-of-range token ids included."""
+    import nanochat_inferonly_lightning_b200 as nc
+
+    V, Dm = 65536, 2176
+    table = rnd((V, Dm), 30, 0.7)
+    tokens = torch.tensor([0, 5, 65535, 5, 12345, 777, 1, 40000], dtype=torch.int32,
+                          device="cuda")
+    out = torch.empty((8, Dm), dtype=torch.bfloat16, device="cuda")
+    G.embed_rmsnorm(out, table, tokens)
+    torch.cuda.synchronize()
+    rows = table[tokens.long()].double()
+    want = rows * torch.rsqrt(rows.square().sum(-1, keepdim=True) / Dm + NORM_EPS)
+    d = (out.double() - want).abs()
+    assert (d <= want.abs() * 2.0 ** -8 + 1e-6).all(), d.max()
+    assert torch.equal(out[1], out[3])
+    assert nc.device_status(reset=True) == 0
+    bad = torch.tensor([3, -1, V], dtype=torch.int32, device="cuda")
+    out3 = torch.full((3, Dm), 1.0, dtype=torch.bfloat16, device="cuda")
+    G.embed_rmsnorm(out3, table, bad)
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) == 0x800  # range check flagged, no out-of-bounds read
+    assert int(out3[1:].count_nonzero()) == 0 and int(out3[0].count_nonzero()) > 0
+
+
+def test_argmax_rows_first_maximum(G):
+    """nc_argmax_rows: the first maximum of each row (src/engine.cpp:88-95, strict '>'), with
+    ties planted at several distances (same thread, same warp, other warps, first and last
+    column) and rows that are constant."""
+    R, C = 12, 65536
+    logits = rnd((R, C), 31, 3.0)
+    top = 40.0
+    plants = {0: [7, 3], 1: [100, 9000], 2: [65535, 0], 3: [8191, 8192], 4: [64000, 64001],
+              5: [12, 13, 14], 6: [70, 30000, 65000], 7: [65535]}
+    for r, cols in plants.items():
+        for c in cols:
+            logits[r, c] = top
+    logits[8] = 1.5  # constant row: index 0
+    logits[9, :] = -2.0
+    logits[9, 4097] = -1.0
+    out = torch.empty(R, dtype=torch.int32, device="cuda")
+    G.argmax_rows(out, logits)
+    torch.cuda.synchronize()
+    want = torch.argmax(logits.float(), dim=-1)  # first occurrence of the maximum
+    assert torch.equal(out.long(), want)
+    assert int(out[0]) == 3 and int(out[2]) == 0 and int(out[8]) == 0 and int(out[9]) == 4097
