@@ -57,6 +57,8 @@ SIGNATURES = {
                                    c_float, c_void_p]),
     "nc_embed_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "nc_argmax_rows": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "nc_sample_rows": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_float,
+                               c_void_p, c_void_p]),
     "nc_gemm_skinny": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_int, c_float, c_int, c_int, c_void_p]),
 }

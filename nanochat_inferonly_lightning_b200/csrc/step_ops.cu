@@ -2,8 +2,9 @@
 // library:
 //  * the embedding gather fused with the RMSNorm that follows it (reference
 //    kernels/ops.cu:9-20 then kernels/rmsnorm.cu:9-56, called at src/model.cpp:158-162);
-//  * greedy sampling, the first maximum of each row of logits (src/engine.cpp:88-95), on the
-//    device so the token never leaves it between steps.
+//  * sampling on the device, so the token never leaves it between steps: greedy (the first
+//    maximum of each row, src/engine.cpp:88-95) and temperature / top-k / top-p sampling
+//    (src/engine.cpp:62-131) with the uniform draw supplied by the caller.
 #include <cstdint>
 
 #include "../../include/nanochat_attn.h"
@@ -124,6 +125,230 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// Sampling (src/engine.cpp:88-131) on the device, one CTA of 1024 threads per row; thread t
+// owns the contiguous slice [t * ept, (t + 1) * ept) of the row, so thread order is index
+// order.
+// ---------------------------------------------------------------------------------------
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleMaxK = 1024;
+
+// bf16 bits -> 16-bit key ordered like the value (larger value, larger key); -0 counts as +0.
+__device__ __forceinline__ uint32_t order_key(uint32_t h) {
+    if (h == 0x8000u) h = 0u;
+    return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+__device__ __forceinline__ float key_value(uint32_t key) {
+    const uint32_t h = (key & 0x8000u) ? (key & 0x7FFFu) : (~key & 0xFFFFu);
+    return __uint_as_float(h << 16);
+}
+
+// Exclusive prefix sum of one int per thread over the block (1024 threads); *total gets the sum.
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_sums[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_sums[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int base = warp > 0 ? warp_sums[warp - 1] : 0;
+    *total = warp_sums[31];
+    __syncthreads();  // warp_sums is reused by the next call
+    return base + x - v;
+}
+
+struct SampleSmem {
+    unsigned long long cand[kSampleMaxK];  // (key << 32) | (0xFFFFFFFF - index)
+    float q[kSampleMaxK];                  // normalised probability of each candidate
+    int hist[256];
+    int warp_sums[32];
+    float fred[32];
+    int b1, above1, kstar, c_gt;
+};
+
+__global__ void __launch_bounds__(kSampleThreads)
+    sample_rows_kernel(int* __restrict__ out, const bf16* __restrict__ logits, int vocab,
+                       float temperature, int top_k, float top_p,
+                       const float* __restrict__ uniforms) {
+    __shared__ SampleSmem sm;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bf16* row = logits + (size_t)blockIdx.x * vocab;
+    const int ept = (((vocab + kSampleThreads - 1) / kSampleThreads) + 7) & ~7;
+    const int c0 = min(tid * ept, vocab), c1 = min(c0 + ept, vocab);
+
+    // 1. maximum logit (Engine::sample :99)
+    float mx = -INFINITY;
+    for (int c = c0; c < c1; c += 8) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) sm.fred[warp] = mx;
+    __syncthreads();
+    mx = sm.fred[0];
+    for (int w = 1; w < 32; ++w) mx = fmaxf(mx, sm.fred[w]);
+    __syncthreads();
+    // 2. sum of expf((l - max) / T) over the row (:101-106)
+    float sum = 0.f;
+    for (int c = c0; c < c1; c += 8) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += expf((f[e] - mx) / temperature);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if (lane == 0) sm.fred[warp] = sum;
+    // 3. the k-th largest key: two 8-bit histogram passes (radix select)
+    for (int i = tid; i < 256; i += kSampleThreads) sm.hist[i] = 0;
+    __syncthreads();
+    sum = 0.f;
+    for (int w = 0; w < 32; ++w) sum += sm.fred[w];
+    for (int c = c0; c < c1; c += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            atomicAdd(&sm.hist[order_key((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu) >> 8], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int cum = 0, b = 255;
+        for (; b > 0; --b) {
+            if (cum + sm.hist[b] >= top_k) break;
+            cum += sm.hist[b];
+        }
+        sm.b1 = b;
+        sm.above1 = cum;
+    }
+    __syncthreads();
+    const int b1 = sm.b1;
+    for (int i = tid; i < 256; i += kSampleThreads) sm.hist[i] = 0;
+    __syncthreads();
+    for (int c = c0; c < c1; c += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t key = order_key((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            if ((int)(key >> 8) == b1) atomicAdd(&sm.hist[key & 0xFF], 1);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int cum = sm.above1, b = 255;
+        for (; b > 0; --b) {
+            if (cum + sm.hist[b] >= top_k) break;
+            cum += sm.hist[b];
+        }
+        sm.kstar = (b1 << 8) | b;
+        sm.c_gt = cum;
+    }
+    __syncthreads();
+    // 4. gather the k candidates: every key above K*, and the lowest-index ties at K*
+    const uint32_t kstar = (uint32_t)sm.kstar;
+    const int c_gt = sm.c_gt, need = top_k - c_gt;
+    int n_gt = 0, n_eq = 0;
+    for (int c = c0; c < c1; c += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t key = order_key((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            n_gt += key > kstar;
+            n_eq += key == kstar;
+        }
+    }
+    int tot;
+    int slot_gt = block_exclusive_scan(n_gt, sm.warp_sums, &tot);
+    int rank_eq = block_exclusive_scan(n_eq, sm.warp_sums, &tot);
+    int P = 1;
+    while (P < top_k) P <<= 1;
+    for (int i = tid; i < P; i += kSampleThreads) sm.cand[i] = 0ull;
+    __syncthreads();
+    for (int c = c0; c < c1; c += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t key = order_key((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            const unsigned long long ck =
+                ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(c + e));
+            if (key > kstar) {
+                sm.cand[slot_gt++] = ck;
+            } else if (key == kstar) {
+                if (rank_eq < need) sm.cand[c_gt + rank_eq] = ck;
+                ++rank_eq;
+            }
+        }
+    }
+    __syncthreads();
+    // 5. bitonic sort, descending: larger value first, equal values by ascending index
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < P; i += kSampleThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long a = sm.cand[i], b = sm.cand[j];
+                    if (desc ? (a < b) : (a > b)) {
+                        sm.cand[i] = b;
+                        sm.cand[j] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // 6. the candidates' normalised probabilities (p = expf(scaled) / sum, :103-110), then
+    // top-p, renormalisation and the draw with the reference's sequential fp32 sums
+    for (int i = tid; i < top_k; i += kSampleThreads)
+        sm.q[i] = expf((key_value((uint32_t)(sm.cand[i] >> 32)) - mx) / temperature) / sum;
+    __syncthreads();
+    if (tid == 0) {
+        int n = top_k;
+        if (top_p < 1.0f) {
+            float cs = 0.f;
+            for (int i = 0; i < n; ++i) {
+                cs += sm.q[i];
+                if (cs > top_p) {
+                    n = i + 1;
+                    break;
+                }
+            }
+        }
+        float s2 = 0.f;
+        for (int i = 0; i < n; ++i) s2 += sm.q[i];
+        const float r = uniforms[blockIdx.x];
+        float cs = 0.f;
+        int chosen = n - 1;
+        for (int i = 0; i < n; ++i) {
+            cs += sm.q[i] / s2;
+            if (r < cs) {
+                chosen = i;
+                break;
+            }
+        }
+        out[blockIdx.x] = (int)(0xFFFFFFFFu - (uint32_t)(sm.cand[chosen] & 0xFFFFFFFFull));
+    }
+}
+
 }  // namespace
 
 }  // namespace nc
@@ -156,6 +381,22 @@ int nc_argmax_rows(int* out, const void* logits, int rows, int cols, cudaStream_
     if (reinterpret_cast<uintptr_t>(logits) & 15) return NC_ERR_MISALIGNED;
     argmax_rows_kernel<<<rows, kArgmaxThreads, 0, stream>>>(out, static_cast<const bf16*>(logits),
                                                             cols);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
+}
+
+int nc_sample_rows(int* out, const void* logits, int rows, int vocab, float temperature,
+                   int top_k, float top_p, const float* uniforms, cudaStream_t stream) {
+    using namespace nc;
+    if (rows < 0 || vocab < 8 || (vocab & 7) || !(temperature >= 0.f)) return NC_ERR_INVALID_ARG;
+    if (rows == 0) return NC_OK;
+    if (!out || !logits) return NC_ERR_INVALID_ARG;
+    if (reinterpret_cast<uintptr_t>(logits) & 15) return NC_ERR_MISALIGNED;
+    if (temperature == 0.f) return nc_argmax_rows(out, logits, rows, vocab, stream);
+    if (top_k < 1 || top_k > kSampleMaxK || top_k >= vocab || !(top_p > 0.f) || !uniforms)
+        return NC_ERR_INVALID_ARG;
+    sample_rows_kernel<<<rows, kSampleThreads, 0, stream>>>(
+        out, static_cast<const bf16*>(logits), vocab, temperature, top_k, top_p, uniforms);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }

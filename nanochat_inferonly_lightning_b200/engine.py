@@ -78,10 +78,18 @@ def logits_of(w, x):
 
 
 class BatchedEngine:
-    """`batch` sequences, each with KV caches of `max_len` rows per layer."""
+    """`batch` sequences, each with KV caches of `max_len` rows per layer.  temperature 0 is
+    greedy decoding; otherwise each step samples with temperature / top_k / top_p as
+    Engine::sample does (src/engine.cpp:62-131), from uniform draws made on the device (torch's
+    CUDA generator, seeded with `seed`), so sampling stays inside the captured step."""
 
-    def __init__(self, weights, batch, max_len, device="cuda"):
+    def __init__(self, weights, batch, max_len, device="cuda", temperature=0.0, top_k=50,
+                 top_p=0.9, seed=None):
         self.w, self.B, self.max_len = weights, batch, max_len
+        self.temperature, self.top_k, self.top_p = float(temperature), int(top_k), float(top_p)
+        if seed is not None:
+            torch.cuda.manual_seed(seed)
+        self.uniforms = torch.zeros(batch, dtype=torch.float32, device=device)
         attn.init_rope_tables()
         shape = (batch, max_len, N_HEAD, HEAD_DIM)
         self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
@@ -152,7 +160,12 @@ class BatchedEngine:
             G.gemm_skinny(x, h, l["down"], residual=x)                   # :153
         # final RMSNorm, LM head, soft cap (:170-177); logits [B, VOCAB] kept for inspection
         G.gemm_skinny(self.logits, x, w.lm_head, flags=G.NORM_INPUT | G.TANH_CAP, cap=LOGIT_CAP)
-        G.argmax_rows(self.tok, self.logits)  # greedy choice (src/engine.cpp:88-95)
+        if self.temperature == 0.0:
+            G.argmax_rows(self.tok, self.logits)  # greedy choice (src/engine.cpp:88-95)
+        else:
+            torch.rand(self.B, out=self.uniforms)
+            G.sample_rows(self.tok, self.logits, self.temperature, self.top_k, self.top_p,
+                          self.uniforms)
 
     def capture(self):
         """Capture one decode step in a CUDA graph (after one eager warm-up step, which also

@@ -80,3 +80,21 @@ def argmax_rows(out, logits, stream=None):
     _lib.check("nc_argmax_rows",
                lib.nc_argmax_rows(_ptr(out), _ptr(logits), rows, cols, _stream(stream)))
     return out
+
+
+def sample_rows(out, logits, temperature, top_k, top_p, uniforms, stream=None):
+    """Engine::sample (src/engine.cpp:62-131) on the device: out[r] (int32) drawn from
+    logits[r] (bf16 [rows, vocab]) with temperature, top-k (1..1024) and top-p, using the
+    uniform draw uniforms[r] (float32 CUDA tensor [rows]); temperature 0 is greedy."""
+    _bf16(logits)
+    if out.dtype != torch.int32:
+        raise TypeError(f"out must be int32, got {out.dtype}")
+    if uniforms is not None and uniforms.dtype != torch.float32:
+        raise TypeError(f"uniforms must be float32, got {uniforms.dtype}")
+    rows, vocab = logits.shape
+    lib = _lib.load()
+    _lib.check("nc_sample_rows",
+               lib.nc_sample_rows(_ptr(out), _ptr(logits), rows, vocab, ctypes.c_float(temperature),
+                                  int(top_k), ctypes.c_float(top_p), _ptr(uniforms),
+                                  _stream(stream)))
+    return out

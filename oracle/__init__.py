@@ -39,6 +39,8 @@ def oracle():
         lib.orc_rope_qknorm_append.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P, _P]
         lib.orc_flash_attention.argtypes = [_P, _P, _P, _P, _I, _I, _I, _F, _I]
         lib.orc_decode_step.argtypes = [_P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P, _P]
+        lib.orc_sample.argtypes = [_P, _I, _F, _I, _F, _F]
+        lib.orc_sample.restype = _I
         for f in ("orc_rope_tables", "orc_apply_rope", "orc_apply_rope_rmsnorm",
                   "orc_rope_qknorm_append", "orc_flash_attention", "orc_decode_step"):
             getattr(lib, f).restype = None
@@ -114,6 +116,14 @@ def decode_step(q, k_new, v_new, k_caches, v_caches, kv_len, heads, scale):
                              ctypes.cast(kp, _P), ctypes.cast(vp, _P), _ptr(lens), batch, heads,
                              float(scale), _ptr(c), _ptr(s))
     return out, kcs, vcs
+
+
+def sample(logits_row, temperature, top_k, top_p, r):
+    """Engine::sample (src/engine.cpp:88-131) of one bf16 logits row (uint16 bits) with the
+    uniform draw r given; equal probabilities ordered by index."""
+    row = _u16(logits_row)
+    return int(oracle().orc_sample(_ptr(row), row.size, float(temperature), int(top_k),
+                                   float(top_p), float(r)))
 
 
 def reference_kernels():

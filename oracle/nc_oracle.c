@@ -195,3 +195,81 @@ void orc_decode_step(uint16_t* out, const uint16_t* q, const uint16_t* k_new,
                             scale, L - 1);
     }
 }
+
+/* ---------------------------------------------------------------------------------------
+ * Sampling: Engine::sample (src/engine.cpp:88-131) for one row of bf16 logits, converted to
+ * float as the engine's logits are.  temperature == 0: the first maximum (:90-96).  Otherwise,
+ * in the reference's order and with its fp32 sequential sums: scaled = (l - max) / T,
+ * p = expf(scaled), p /= sum (all entries, index order) (:99-110); top_k_filter: the k largest
+ * (:62-68); top_p_filter: sort descending, keep entries up to and including the first whose
+ * running sum exceeds top_p (:70-84); renormalise (:116-119); return the first entry whose
+ * running sum exceeds r (:121-128), else the last.  r is the uniform draw (the reference draws
+ * it from its mt19937).  The reference's std::partial_sort / std::sort leave the order of equal
+ * probabilities unspecified; here equal values are ordered by ascending index.
+ * --------------------------------------------------------------------------------------- */
+typedef struct {
+    float p;
+    int idx;
+} orc_prob;
+
+static int prob_desc(const void* a, const void* b) {
+    const orc_prob* x = (const orc_prob*)a;
+    const orc_prob* y = (const orc_prob*)b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return x->idx - y->idx;
+}
+
+int orc_sample(const uint16_t* logits, int vocab, float temperature, int top_k, float top_p,
+               float r) {
+    if (temperature == 0.0f) {
+        int best = 0;
+        for (int i = 1; i < vocab; i++)
+            if (bf2f(logits[i]) > bf2f(logits[best])) best = i;
+        return best;
+    }
+    orc_prob* probs = (orc_prob*)malloc(sizeof(orc_prob) * (size_t)vocab);
+    float max_logit = bf2f(logits[0]);
+    for (int i = 1; i < vocab; i++)
+        if (bf2f(logits[i]) > max_logit) max_logit = bf2f(logits[i]);
+    float sum = 0.0f;
+    for (int i = 0; i < vocab; i++) {
+        float scaled = (bf2f(logits[i]) - max_logit) / temperature;
+        probs[i].p = expf(scaled);
+        probs[i].idx = i;
+        sum += probs[i].p;
+    }
+    for (int i = 0; i < vocab; i++) probs[i].p /= sum;
+    int n = vocab;
+    if (top_k > 0 && top_k < n) {  /* partial sort: the k largest, in descending order */
+        qsort(probs, (size_t)n, sizeof(orc_prob), prob_desc);
+        n = top_k;
+    }
+    if (top_p < 1.0f) {
+        qsort(probs, (size_t)n, sizeof(orc_prob), prob_desc);
+        float cumsum = 0.0f;
+        int cutoff = n;
+        for (int i = 0; i < n; i++) {
+            cumsum += probs[i].p;
+            if (cumsum > top_p) {
+                cutoff = i + 1;
+                break;
+            }
+        }
+        n = cutoff;
+    }
+    sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += probs[i].p;
+    for (int i = 0; i < n; i++) probs[i].p /= sum;
+    float cumsum = 0.0f;
+    int chosen = probs[n - 1].idx;
+    for (int i = 0; i < n; i++) {
+        cumsum += probs[i].p;
+        if (r < cumsum) {
+            chosen = probs[i].idx;
+            break;
+        }
+    }
+    free(probs);
+    return chosen;
+}

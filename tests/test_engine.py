@@ -91,3 +91,23 @@ def test_decode_steps_match_prefill_recompute(setup):
                 toks[s] = want  # follow the recompute so both stay on the same sequence
                 eng.tok[s] = want
     assert worst < 0.25, worst
+
+
+def test_sampled_decode_in_graph(setup):
+    """Temperature / top-k / top-p sampling inside the captured step (device draws): every
+    sampled token is among the top_k logits of its row, and two engines seeded alike sample the
+    same tokens."""
+    nc, E, w, prompts = setup
+    runs = []
+    for _ in range(2):
+        eng = E.BatchedEngine(w, B, MAX_LEN, temperature=1.0, top_k=20, top_p=0.9, seed=123)
+        eng.prefill(prompts)
+        toks = [eng.capture()]
+        for _ in range(4):
+            t = eng.step().clone()
+            kth = torch.topk(eng.logits.float(), 20, dim=-1).values[:, -1]
+            chosen = eng.logits.float().gather(1, t.long()[:, None])[:, 0]
+            assert bool((chosen >= kth).all())  # within the top 20 (ties at the edge allowed)
+            toks.append(t)
+        runs.append(torch.stack(toks))
+    assert torch.equal(runs[0], runs[1])

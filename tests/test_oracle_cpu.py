@@ -135,3 +135,42 @@ def test_golden_attention():
         got = oracle.flash_attention(g[n + "_q"], g[n + "_k"], g[n + "_v"], seq_q, kv_len, H,
                                      SCALE, off)
         assert_close_bf16(got, g[n + "_out"], what=n)
+
+
+# ------------------------------------------------------------------------------ sampling
+def _sample_intervals(row_u16, T, k, p):
+    """Engine::sample's kept entries and their renormalised running sums, in float64 (for
+    checking the oracle's choices away from the interval edges)."""
+    lf = oracle.bf16_bits_to_f32(row_u16).astype(np.float64)
+    pr = np.exp((lf - lf.max()) / T)
+    pr /= pr.sum()
+    order = sorted(range(len(pr)), key=lambda i: (-pr[i], i))
+    if 0 < k < len(pr):
+        order = order[:k]
+    if p < 1.0:
+        cs = np.cumsum(pr[order])
+        cut = int(np.argmax(cs > p)) + 1 if (cs > p).any() else len(order)
+        order = order[:cut]
+    w = pr[order] / pr[order].sum()
+    return order, np.cumsum(w)
+
+
+def test_oracle_sample_matches_intervals():
+    """orc_sample (Engine::sample, src/engine.cpp:88-131): greedy at temperature 0 is the first
+    maximum; otherwise the draw r picks the entry whose renormalised running-sum interval holds
+    r (checked at interval midpoints, away from fp32 rounding)."""
+    rng = np.random.default_rng(11)
+    V = 4096
+    row = oracle.f32_to_bf16_bits((rng.standard_normal(V) * 2.0).astype(np.float32))
+    row[[17, 900]] = oracle.f32_to_bf16_bits(np.array([9.0, 9.0], np.float32))  # tied maxima
+    assert oracle.sample(row, 0.0, 50, 0.9, 0.5) == 17
+    for T, k, p in [(1.0, 50, 0.9), (0.7, 5, 1.0), (1.5, 200, 0.5), (1.0, 1, 0.9)]:
+        order, cs = _sample_intervals(row, T, k, p)
+        lo = np.concatenate([[0.0], cs[:-1]])
+        for j in range(len(order)):
+            r = 0.5 * (lo[j] + cs[j])
+            if cs[j] - lo[j] < 1e-5:
+                continue
+            assert oracle.sample(row, T, k, p, r) == order[j], (T, k, p, j)
+    # top_k == 1: always the first maximum
+    assert oracle.sample(row, 1.0, 1, 1.0, 0.999) == 17
