@@ -106,6 +106,8 @@ class BatchedEngine:
         self.ws = torch.zeros(attn.decode_workspace_bytes(batch, max_len, N_HEAD),
                               dtype=torch.uint8, device=device)
         self.tok = torch.zeros(batch, dtype=torch.int32, device=device)  # next input token
+        # 1 for a slot holding a live sequence: only those lengths advance in a decode step
+        self.active = torch.zeros(batch, dtype=torch.int32, device=device)
         # decode-step GEMM operands: fused [q; k; v] weights and the activations
         self.wqkv = [torch.cat([l["q"], l["k"], l["v"]], 0) for l in weights.layers]
         bf = dict(dtype=torch.bfloat16, device=device)
@@ -117,35 +119,59 @@ class BatchedEngine:
         self.graph = None
 
     # ------------------------------------------------------------------ prompt
+    def _prompt_pass(self, b, prompt):
+        """Prompt pass of one sequence into slot b's caches (rows [0, P)); returns its first
+        generated token (greedy, as the reference's first step, src/engine.cpp:37-62)."""
+        P = int(prompt.numel())
+        assert 0 < P < self.max_len
+        w = self.w
+        x = rmsnorm(w.embed[prompt])
+        for i, l in enumerate(w.layers):
+            xn = rmsnorm(x)
+            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
+            a = torch.empty_like(q)
+            attn.rope_qknorm_append(q, k, v, self.k[i][b], self.v[i][b], P, N_HEAD, 0)
+            attn.flash_attention(a, q, self.k[i][b], self.v[i][b], P, P, N_HEAD, SCALE, 0)
+            x = torch.addmm(x, a, l["o"].t())
+            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
+            x = torch.addmm(x, h, l["down"].t())
+        return torch.argmax(logits_of(w, x[-1:])[0].float())
+
     def prefill(self, prompts):
-        """prompts: int64 [B, P] token ids; fills the caches and sets the first generated
-        token of every sequence (returned, and kept as the next decode input)."""
+        """prompts: int64 [B, P] token ids; fills the caches of every slot and sets the first
+        generated token of every sequence (returned, and kept as the next decode input)."""
         B, P = prompts.shape
         assert B == self.B and P < self.max_len
-        w = self.w
         first = torch.empty(B, dtype=torch.int64, device=prompts.device)
         for b in range(B):
-            x = rmsnorm(w.embed[prompts[b]])
-            for i, l in enumerate(w.layers):
-                xn = rmsnorm(x)
-                q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
-                a = torch.empty_like(q)
-                attn.rope_qknorm_append(q, k, v, self.k[i][b], self.v[i][b], P, N_HEAD, 0)
-                attn.flash_attention(a, q, self.k[i][b], self.v[i][b], P, P, N_HEAD, SCALE, 0)
-                x = torch.addmm(x, a, l["o"].t())
-                h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
-                x = torch.addmm(x, h, l["down"].t())
-            first[b] = torch.argmax(logits_of(w, x[-1:])[0].float())
+            first[b] = self._prompt_pass(b, prompts[b])
         self.kv_len.fill_(P)
         self.tok.copy_(first)
+        self.active.fill_(1)
         return first
+
+    # ------------------------------------------------------------------ continuous batching
+    def admit(self, slot, prompt):
+        """Starts a new sequence in `slot` between decode steps (continuous batching): its
+        prompt pass runs now, its length and next token are set on the device, and the next
+        step (graph replay included) advances it with the others.  Returns its first token."""
+        first = self._prompt_pass(slot, prompt)
+        self.kv_len[slot] = int(prompt.numel())
+        self.tok[slot] = first
+        self.active[slot] = 1
+        return first
+
+    def retire(self, slot):
+        """Frees `slot`: its length stops advancing (its rows are recomputed and ignored until a
+        new sequence is admitted there)."""
+        self.active[slot] = 0
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self):
         """One greedy step for the whole batch: consumes self.tok, writes the next tokens back
         into self.tok.  Static shapes, device-side lengths: safe to capture."""
         w, x, qkv, a, h = self.w, self.x, self.qkv, self.a, self.h
-        self.kv_len.add_(1)  # the new token sits at row kv_len - 1
+        self.kv_len.add_(self.active)  # a live slot's new token sits at row kv_len - 1
         G.embed_rmsnorm(x, w.embed, self.tok)  # embedding + RMSNorm (:158-162)
         for i, l in enumerate(w.layers):
             # RMSNorm -> Q/K/V (src/model.cpp:110-116)

@@ -111,3 +111,35 @@ def test_sampled_decode_in_graph(setup):
             toks.append(t)
         runs.append(torch.stack(toks))
     assert torch.equal(runs[0], runs[1])
+
+
+def test_continuous_batching(setup):
+    """Sequences join and leave the running batch between graph replays (admit / retire)
+    without re-capturing: a sequence admitted into slot 2 after three steps of slot 0 produces
+    exactly the tokens it produces when it runs alone, slot 0 is unaffected by the newcomer,
+    and a retired slot's length stops advancing."""
+    nc, E, w, prompts = setup
+    a = E.BatchedEngine(w, B, MAX_LEN)
+    slot0 = [int(a.admit(0, prompts[0]))]
+    slot0.append(int(a.capture()[0]))  # one eager step, then the capture
+    for _ in range(2):
+        slot0.append(int(a.step()[0]))
+    slot2 = [int(a.admit(2, prompts[2]))]
+    for _ in range(4):
+        t = a.step().clone()
+        slot0.append(int(t[0]))
+        slot2.append(int(t[2]))
+    a.retire(0)
+    n0 = int(a.kv_len[0])
+    a.step()
+    assert int(a.kv_len[0]) == n0 and int(a.kv_len[2]) == PROMPT + 5
+
+    def alone(slot, n_tokens):
+        e = E.BatchedEngine(w, B, MAX_LEN)
+        toks = [int(e.admit(slot, prompts[slot])), int(e.capture()[slot])]
+        while len(toks) < n_tokens:
+            toks.append(int(e.step()[slot]))
+        return toks
+
+    assert slot2 == alone(2, len(slot2))
+    assert slot0 == alone(0, len(slot0))
