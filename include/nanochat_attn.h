@@ -105,6 +105,22 @@ int nc_decode_attention(void* out, const void* q, const void* k_new, const void*
                         int batch, int heads, float scale, int max_kv_len, int split_len,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* nc_decode_attention over a paged cache.  K and V live in two pools of num_pages pages, each
+ * [page_rows][heads][128] bf16 (page_rows a multiple of 16); row r of sequence b is row
+ * r % page_rows of page page_table[b * pages_per_seq + r / page_rows] (page_table: device
+ * int32 [batch][pages_per_seq], pages_per_seq * page_rows >= max_kv_len).  The new key and
+ * value are appended at row kv_len[b] - 1 through the same table, so the caller maps a page
+ * for that row before the call.  A page id outside [0, num_pages) is not dereferenced: the
+ * access is skipped and bit 0x400 of the device status word is set.  Otherwise as
+ * nc_decode_attention, with the same workspace rules.
+ * Replaces: the contiguous per-layer KVCache buffers (src/model.h:65-73) for decode, so that a
+ * sequence holds only the pages it uses.  No counterpart in the reference. */
+int nc_decode_attention_paged(void* out, const void* q, const void* k_new, const void* v_new,
+                              void* k_pool, void* v_pool, int num_pages, int page_rows,
+                              const int* page_table, int pages_per_seq, const int* kv_len,
+                              int batch, int heads, float scale, int max_kv_len, int split_len,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* nc_decode_attention for a call that directly follows, on the same stream, a kernel that
  * writes none of the caches, kv_len or the two pointer arrays (typically the Q/K/V projection
  * of nc_gemm_skinny).  Small batches (the per-head layout) then launch as a programmatic

@@ -8,12 +8,12 @@ Importing it does not load the library; the first call does, and raises if it is
 from ._lib import LIB_PATH, NcError, load
 from . import gemm
 from .attn import (HEAD_DIM, ROPE_MAX_SEQ, KVCache, apply_rope, apply_rope_rmsnorm,
-                   decode_attention, decode_workspace_bytes, device_status, flash_attention,
+                   decode_attention, decode_attention_paged, decode_workspace_bytes, device_status, flash_attention,
                    init_rope_tables, prefill_attention_batched, rope_qknorm_append)
 
 __all__ = [
     "LIB_PATH", "NcError", "load", "HEAD_DIM", "ROPE_MAX_SEQ", "KVCache", "apply_rope",
-    "apply_rope_rmsnorm", "decode_attention", "decode_workspace_bytes", "device_status",
+    "apply_rope_rmsnorm", "decode_attention", "decode_attention_paged", "decode_workspace_bytes", "device_status",
     "flash_attention", "init_rope_tables", "prefill_attention_batched", "rope_qknorm_append",
     "gemm",
 ]

@@ -31,6 +31,10 @@ SIGNATURES = {
     "nc_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int,
                                     c_void_p, c_size_t, c_void_p]),
+    "nc_decode_attention_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
+                                          c_int, c_int, c_float, c_int, c_int, c_void_p,
+                                          c_size_t, c_void_p]),
     "nc_decode_attention_overlap": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p, c_int, c_int, c_float, c_int,
                                             c_int, c_void_p, c_size_t, c_void_p]),

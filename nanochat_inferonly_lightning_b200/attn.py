@@ -108,6 +108,28 @@ def decode_attention(out, q, k_new, v_new, k_ptrs, v_ptrs, kv_len, heads, scale,
                                   _stream(stream)))
 
 
+def decode_attention_paged(out, q, k_new, v_new, k_pool, v_pool, page_table, kv_len, heads,
+                           scale, max_kv_len, workspace, split_len=0, stream=None):
+    """Batched decode step over a paged cache (nc_decode_attention_paged).
+
+    k_pool/v_pool: bf16 CUDA tensors [num_pages, page_rows, heads, 128]; page_table: int32 CUDA
+    tensor [B, pages_per_seq] of page ids; kv_len: int32 CUDA tensor [B]."""
+    _bf16(out, q, k_new, v_new, k_pool, v_pool)
+    if page_table.dtype != torch.int32 or page_table.dim() != 2:
+        raise TypeError("page_table must be an int32 tensor [batch, pages_per_seq]")
+    batch = int(kv_len.numel())
+    num_pages, page_rows = int(k_pool.shape[0]), int(k_pool.shape[1])
+    lib = _lib.load()
+    _lib.check("nc_decode_attention_paged",
+               lib.nc_decode_attention_paged(_ptr(out), _ptr(q), _ptr(k_new), _ptr(v_new),
+                                             _ptr(k_pool), _ptr(v_pool), num_pages, page_rows,
+                                             _ptr(page_table), int(page_table.shape[1]),
+                                             _ptr(kv_len), batch, heads, float(scale),
+                                             max_kv_len, split_len, _ptr(workspace),
+                                             workspace.numel() if workspace is not None else 0,
+                                             _stream(stream)))
+
+
 def prefill_attention_batched(out, q, k_slab, v_slab, seq_stride, rows_per_seq, kv_offset,
                               seq_q, heads, scale, stream=None):
     """Batched chunked prefill over caches that are slices of one slab (seq_stride elements

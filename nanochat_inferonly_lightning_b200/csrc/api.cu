@@ -142,11 +142,19 @@ int rope_common(RopeMode mode, void* x, const void* k, const void* v, void* kc, 
     return e == cudaSuccess ? NC_OK : cuda_fail(e);
 }
 
+// Paged cache of nc_decode_attention_paged (see DecodeArgs).
+struct PagedKV {
+    void* k_pool;
+    void* v_pool;
+    const int* page_table;
+    int num_pages, page_rows, pages_per_seq;
+};
+
 int decode_common(void* out, const void* q, const void* k_new, const void* v_new,
                   void* const* k_caches, void* const* v_caches, void* k_single, void* v_single,
                   const int* kv_len, int n_visible_single, int batch, int heads, float scale,
                   int max_kv_len, int split_len, void* ws, size_t ws_bytes,
-                  cudaStream_t stream, int overlap = 0) {
+                  cudaStream_t stream, int overlap = 0, const PagedKV* pg = nullptr) {
     // The decode kernel runs one warp per head plus a producer warp (<= 1024 threads).
     if (batch < 0 || heads < 1 || heads > 31 || max_kv_len < 0) return NC_ERR_INVALID_ARG;
     if (batch == 0) return NC_OK;
@@ -157,6 +165,13 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
         return NC_ERR_MISALIGNED;
     if (split_len < 0 || (split_len % 16) != 0) return NC_ERR_INVALID_ARG;
     if (k_new && max_kv_len > kRopeMaxSeq) return NC_ERR_RANGE;
+    if (pg) {
+        if (!pg->k_pool || !pg->v_pool || !pg->page_table || !kv_len) return NC_ERR_INVALID_ARG;
+        if (pg->page_rows < 16 || pg->page_rows % 16 || pg->num_pages < 1 ||
+            pg->pages_per_seq < 1 || (long long)pg->pages_per_seq * pg->page_rows < max_kv_len)
+            return NC_ERR_INVALID_ARG;
+        if (!aligned16(pg->k_pool) || !aligned16(pg->v_pool)) return NC_ERR_MISALIGNED;
+    }
     const int T = split_len ? split_len : auto_split_len(batch, std::max(max_kv_len, 1));
     const int max_splits = std::max(1, (max_kv_len + T - 1) / T);
     if (max_splits > 65535) return NC_ERR_INVALID_ARG;
@@ -181,6 +196,14 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
     a.batch = batch;
     a.heads = heads;
     a.q_raw = k_new != nullptr;
+    if (pg) {
+        a.k_pool = static_cast<bf16*>(pg->k_pool);
+        a.v_pool = static_cast<bf16*>(pg->v_pool);
+        a.page_table = pg->page_table;
+        a.page_rows = pg->page_rows;
+        a.pages_per_seq = pg->pages_per_seq;
+        a.num_pages = pg->num_pages;
+    }
     a.head_layout = decode_use_head_layout(batch, max_kv_len, split_len) ? 1 : 0;
     a.overlap = overlap && a.head_layout ? 1 : 0;
     a.scale_log2 = scale * kLog2e;
@@ -374,6 +397,17 @@ int nc_decode_attention(void* out, const void* q, const void* k_new, const void*
     return decode_common(out, q, k_new, v_new, k_caches, v_caches, nullptr, nullptr, kv_len, 0,
                          batch, heads, scale, max_kv_len, split_len, workspace,
                          workspace_bytes, stream);
+}
+
+int nc_decode_attention_paged(void* out, const void* q, const void* k_new, const void* v_new,
+                              void* k_pool, void* v_pool, int num_pages, int page_rows,
+                              const int* page_table, int pages_per_seq, const int* kv_len,
+                              int batch, int heads, float scale, int max_kv_len, int split_len,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    const PagedKV pg{k_pool, v_pool, page_table, num_pages, page_rows, pages_per_seq};
+    return decode_common(out, q, k_new, v_new, nullptr, nullptr, nullptr, nullptr, kv_len, 0,
+                         batch, heads, scale, max_kv_len, split_len, workspace,
+                         workspace_bytes, stream, 0, &pg);
 }
 
 int nc_decode_attention_overlap(void* out, const void* q, const void* k_new, const void* v_new,

@@ -73,8 +73,28 @@ __device__ __forceinline__ int raw_len(const DecodeArgs& a, int b) {
     return a.kv_len ? a.kv_len[b] : a.n_visible_single;
 }
 
+// Start of cache row r of sequence b, K (v == false) or V.  Contiguous caches: the sequence's
+// base + r rows.  Paged caches: the row's page from the page table; a page id outside
+// [0, num_pages) sets kStatusBounds and yields null (callers then skip the access).
+template <bool PAGED>
+__device__ __forceinline__ bf16* kv_row(const DecodeArgs& a, bool v, int b, int r) {
+    const size_t rowstride = (size_t)a.heads * kHeadDim;
+    if (PAGED) {
+        const int page = a.page_table[(size_t)b * a.pages_per_seq + r / a.page_rows];
+        if (page < 0 || page >= a.num_pages) {
+            atomicOr(a.status, kStatusBounds);
+            return nullptr;
+        }
+        return (v ? a.v_pool : a.k_pool) +
+               ((size_t)page * a.page_rows + (r % a.page_rows)) * rowstride;
+    }
+    bf16* base = v ? (a.v_cache ? a.v_cache[b] : a.v_single)
+                   : (a.k_cache ? a.k_cache[b] : a.k_single);
+    return base + (size_t)r * rowstride;
+}
+
 // MAX_THREADS selects the register budget: (heads + 1) warps must fit in it.
-template <int MAX_THREADS>
+template <int MAX_THREADS, bool PAGED>
 __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, int rows_per_stage) {
     // A GEMM launched after this kernel with programmatic dependent launch (the output
     // projection) may start streaming its weights now; it waits for this grid to complete
@@ -140,10 +160,12 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 const int ke = max(0, min(L, ks + a.split_len));
                 const bool owns_new = a.k_new != nullptr && L > 0 && ke == L;
                 const int ke_s = owns_new ? ke - 1 : ke;  // the new key comes from registers
-                const bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
-                const bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
-                for (int r0 = ks, first = 1; first || r0 < ke_s; r0 += R, first = 0) {
-                    const int nr = max(0, min(R, ke_s - r0));
+                // Stages of up to R rows; with a paged cache a stage never crosses a page.
+                for (int r0 = ks, first = 1, nr = 0; first || r0 < ke_s; r0 += nr, first = 0) {
+                    nr = max(0, min(R, ke_s - r0));
+                    if (PAGED) nr = min(nr, a.page_rows - r0 % a.page_rows);
+                    const bf16* krow = nr > 0 ? kv_row<PAGED>(a, false, b, r0) : nullptr;
+                    const bf16* vrow = nr > 0 ? kv_row<PAGED>(a, true, b, r0) : nullptr;
                     int s;
                     if (!(ok = acquire_slot(s))) break;
                     StageHdr& hd = tail->hdr[s];
@@ -151,17 +173,17 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                     hd.first = r0;
                     hd.nrows = nr;
                     hd.item_first = first;
-                    hd.item_last = (r0 + R >= ke_s) ? 1 : 0;
+                    hd.item_last = (r0 + nr >= ke_s) ? 1 : 0;
                     hd.split = split;
                     hd.n_splits = n_splits;
                     hd.L = L;
                     uint8_t* dst = smem + (size_t)s * stage_bytes;
-                    if (nr > 0) {
+                    if (nr > 0 && krow && vrow) {
                         mbar_arrive_expect_tx(&tail->full[s], 2u * nr * rowbytes);
-                        bulk_g2s(dst, kb + (size_t)r0 * rowstride, nr * rowbytes, &tail->full[s]);
-                        bulk_g2s(dst + (size_t)R * rowbytes, vb + (size_t)r0 * rowstride,
-                                 nr * rowbytes, &tail->full[s]);
+                        bulk_g2s(dst, krow, nr * rowbytes, &tail->full[s]);
+                        bulk_g2s(dst + (size_t)R * rowbytes, vrow, nr * rowbytes, &tail->full[s]);
                     } else {
+                        hd.nrows = 0;  // nothing copied (no rows, or a bad page id)
                         mbar_arrive(&tail->full[s]);
                     }
                     ++n;
@@ -327,14 +349,16 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
                 // New token (position L-1): RoPE + QK-norm of its key, append K and V to the
                 // cache, add its contribution (lanes of half 0 only).
                 const int pos = L - 1;
-                bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
-                bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
                 const uint4 kn = new_k;  // prepared at the start of this item
                 const uint4 vr = new_v;
-                const size_t coff = (size_t)pos * rowstride + (size_t)h * kHeadDim + 8 * sub;
                 if (half == 0) {
-                    *reinterpret_cast<uint4*>(kb + coff) = kn;
-                    *reinterpret_cast<uint4*>(vb + coff) = vr;
+                    bf16* kd = kv_row<PAGED>(a, false, b, pos);
+                    bf16* vd = kv_row<PAGED>(a, true, b, pos);
+                    const size_t hoff = (size_t)h * kHeadDim + 8 * sub;
+                    if (kd && vd) {
+                        *reinterpret_cast<uint4*>(kd + hoff) = kn;
+                        *reinterpret_cast<uint4*>(vd + hoff) = vr;
+                    }
                 }
                 float sc = dot8(qf, kn);
                 sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 8);
@@ -460,6 +484,7 @@ __global__ void __launch_bounds__(MAX_THREADS, 1) decode_kernel(DecodeArgs a, in
 // (fused RoPE + QK-norm of q and of the new key, online softmax in log2 units, four rows per
 // half-warp step); the four warps merge through shared memory, and, with several splits, the
 // last split of each (sequence, head) to finish combines them (per-head ticket, self-resetting).
+template <bool PAGED>
 __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     asm volatile("griddepcontrol.launch_dependents;");  // as in decode_kernel
     __shared__ float sm_o[4][kHeadDim];
@@ -477,8 +502,6 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     // is written by the kernel that precedes an overlapped launch (a.overlap), so they are
     // read before griddepcontrol.wait; the query and the new key and value come after it.
     const int Lraw = raw_len(a, b);
-    bf16* kb = a.k_cache ? a.k_cache[b] : a.k_single;
-    bf16* vb = a.v_cache ? a.v_cache[b] : a.v_single;
     const int L = min(Lraw, a.max_kv_len);
     const int T = a.split_len;
     const int n_splits = L > 0 ? (L + T - 1) / T : 1;
@@ -502,12 +525,16 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     // This warp's rows [w0, w1); half-warp `half` takes w0 + half, w0 + half + 2, ...
     const int w0 = ks + 16 * warp;
     const int w1 = min(ke_s, w0 + 16);
+    // The warp's 16 rows are consecutive in the cache (a paged cache's pages hold a multiple
+    // of 16 rows, and w0 is a multiple of 16): one base per warp.
+    const bf16* kb = w0 < w1 ? kv_row<PAGED>(a, false, b, w0) : nullptr;
+    const bf16* vb = w0 < w1 ? kv_row<PAGED>(a, true, b, w0) : nullptr;
     uint4 kr[8], vr[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int r = w0 + 2 * i + half;
-        if (r < w1) {
-            const size_t off = (size_t)r * rowstride + (size_t)h * kHeadDim + 8 * sub;
+        if (r < w1 && kb && vb) {
+            const size_t off = (size_t)(r - w0) * rowstride + (size_t)h * kHeadDim + 8 * sub;
             kr[i] = *reinterpret_cast<const uint4*>(kb + off);
             vr[i] = *reinterpret_cast<const uint4*>(vb + off);
         } else {
@@ -537,10 +564,14 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
         float y[8];
         rope_norm_row(a.rope_cs, kraw, sub, hmask, L - 1, true, y);
         new_k = f32_to_bf16x8(y);
-        const size_t coff = (size_t)(L - 1) * rowstride + (size_t)h * kHeadDim + 8 * sub;
         if (half == 0) {
-            *reinterpret_cast<uint4*>(kb + coff) = new_k;
-            *reinterpret_cast<uint4*>(vb + coff) = new_v;
+            bf16* kd = kv_row<PAGED>(a, false, b, L - 1);
+            bf16* vd = kv_row<PAGED>(a, true, b, L - 1);
+            const size_t hoff = (size_t)h * kHeadDim + 8 * sub;
+            if (kd && vd) {
+                *reinterpret_cast<uint4*>(kd + hoff) = new_k;
+                *reinterpret_cast<uint4*>(vd + hoff) = new_v;
+            }
         }
     }
 
@@ -777,14 +808,16 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
     if (!attr[dev]) {
         size_t most = 0;  // the opt-in must cover every head count the kernel accepts
         for (int hh = 1; hh <= 31; ++hh) most = std::max(most, decode_smem_bytes(hh));
-        e = cudaFuncSetAttribute(decode_kernel<576>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)most);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_kernel<1024>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most);
+        e = cudaSuccess;
+        for (auto fn : {decode_kernel<576, false>, decode_kernel<1024, false>,
+                        decode_kernel<576, true>, decode_kernel<1024, true>})
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)most);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
+    const bool paged = a.page_table != nullptr;
     if (a.head_layout) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)a.max_splits, (unsigned)a.heads, (unsigned)a.batch);
@@ -795,17 +828,21 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         at[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = at;
         cfg.numAttrs = a.overlap ? 1 : 0;
-        return cudaLaunchKernelEx(&cfg, decode_head_kernel, a);
+        return paged ? cudaLaunchKernelEx(&cfg, decode_head_kernel<true>, a)
+                     : cudaLaunchKernelEx(&cfg, decode_head_kernel<false>, a);
     }
     const long long items = (long long)a.max_splits * a.batch;
     const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(items, sms[dev]));
     const int threads = (a.heads + 1) * 32;  // one warp per head + the producer warp
-    if (threads <= 576)
-        decode_kernel<576><<<grid, threads, decode_smem_bytes(a.heads), stream>>>(
-            a, decode_rows_per_stage(a.heads));
-    else
-        decode_kernel<1024><<<grid, threads, decode_smem_bytes(a.heads), stream>>>(
-            a, decode_rows_per_stage(a.heads));
+    const size_t smem = decode_smem_bytes(a.heads);
+    const int R = decode_rows_per_stage(a.heads);
+    if (threads <= 576) {
+        if (paged) decode_kernel<576, true><<<grid, threads, smem, stream>>>(a, R);
+        else decode_kernel<576, false><<<grid, threads, smem, stream>>>(a, R);
+    } else {
+        if (paged) decode_kernel<1024, true><<<grid, threads, smem, stream>>>(a, R);
+        else decode_kernel<1024, false><<<grid, threads, smem, stream>>>(a, R);
+    }
     return cudaGetLastError();
 }
 

@@ -204,6 +204,15 @@ struct DecodeArgs {
     int batch;
     int heads;
     int q_raw;                    // 1: q is pre-RoPE and gets RoPE + QK-norm in the kernel
+    // Paged cache (page_table != null): row r of sequence b is row r % page_rows of page
+    // page_table[b * pages_per_seq + r / page_rows] of k_pool / v_pool, pools laid out
+    // [num_pages][page_rows][heads][128]; k_cache / v_cache / k_single are then unused.
+    bf16* k_pool;
+    bf16* v_pool;
+    const int* page_table;
+    int page_rows;                // multiple of 16
+    int pages_per_seq;
+    int num_pages;
     int head_layout;              // 1: per-head layout (decode_use_head_layout)
     int overlap;                  // 1: per-head layout launched as a programmatic dependent
                                   // launch; cache rows, lengths and pointer tables are read

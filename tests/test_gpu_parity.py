@@ -290,6 +290,79 @@ def test_decode_batched_streaming_layout(nc):
     _decode_batch(nc, [1, 5, 16, 33, 64, 128, 300, 511, 777, 1024, 1500, 2047], 0, seed=450)
 
 
+@pytest.mark.parametrize("lens,page_rows,heads,split_len", [
+    ([1, 2, 17, 100, 513, 1200], 64, H, 0),          # per-head layout
+    ([300, 7, 64, 65], 16, H, 0),                     # per-head layout, small pages
+    ([1, 5, 16, 33, 64, 128, 300, 511, 777, 1024, 1500, 2047], 48, H, 0),  # streaming
+    ([40, 700, 1300], 128, H, 80),                    # streaming, explicit split
+    ([3, 90, 250, 600, 1000, 11, 77, 500, 333], 16, 20, 0),  # streaming, 6-row stages
+])
+def test_decode_paged(nc, lens, page_rows, heads, split_len):
+    """nc_decode_attention_paged: K/V rows live in shuffled pages of two pools; the new key and
+    value are appended through the page table.  Output against the oracle on the equivalent
+    contiguous caches, appended rows in the right pages, spare pages untouched."""
+    B, max_len = len(lens), max(lens)
+    pps = -(-max_len // page_rows)
+    num_pages = B * pps + 3
+    rng = np.random.default_rng(700 + page_rows)
+    perm = rng.permutation(num_pages).astype(np.int32)
+    table = perm[:B * pps].reshape(B, pps)
+    q = randn_u16((B, heads, D), 710)
+    kn = randn_u16((B, heads, D), 711)
+    vn = randn_u16((B, heads, D), 712)
+    kcs = [normed(randn_u16((pps * page_rows, heads, D), 720 + b), 0) for b in range(B)]
+    vcs = [randn_u16((pps * page_rows, heads, D), 760 + b) for b in range(B)]
+    want, wkc, wvc = oracle.decode_step(q, kn, vn, kcs, vcs, lens, heads, SCALE)
+    kpool = np.zeros((num_pages, page_rows, heads, D), np.uint16)
+    vpool = np.zeros_like(kpool)
+    for b in range(B):
+        for j in range(pps):
+            kpool[table[b, j]] = kcs[b][j * page_rows:(j + 1) * page_rows]
+            vpool[table[b, j]] = vcs[b][j * page_rows:(j + 1) * page_rows]
+    tk, tv = dev(kpool), dev(vpool)
+    pt = torch.tensor(table, dtype=torch.int32, device="cuda")
+    lt = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(nc.decode_workspace_bytes(B, max_len, heads, split_len), dtype=torch.uint8,
+                     device="cuda")
+    out = torch.empty((B, heads * D), dtype=torch.bfloat16, device="cuda")
+    nc.decode_attention_paged(out, dev(q), dev(kn), dev(vn), tk, tv, pt, lt, heads, SCALE,
+                              max_len, ws, split_len=split_len)
+    torch.cuda.synchronize()
+    assert_close_bf16(bf16_to_u16(out).reshape(B, heads * D), want, what=f"paged {lens}")
+    gk, gv = bf16_to_u16(tk), bf16_to_u16(tv)
+    for b, L in enumerate(lens):
+        pg, row = table[b, (L - 1) // page_rows], (L - 1) % page_rows
+        assert ulp_diff_bf16(gk[pg, row], wkc[b][L - 1]).max() <= 1, f"appended K, seq {b}"
+        assert np.array_equal(gv[pg, row], wvc[b][L - 1]), f"appended V, seq {b}"
+    spare = perm[B * pps:]
+    assert not gk[spare].any() and not gv[spare].any()
+    assert nc.device_status(reset=True) == 0
+
+
+def test_decode_paged_bad_page_id_is_flagged(nc):
+    """A page id outside the pool is not dereferenced: the call completes, the status word gets
+    the bounds bit, and the pool is not written."""
+    B, page_rows, pps, num_pages = 2, 16, 4, 8
+    lens = [40, 50]
+    table = np.array([[0, 1, 2, 3], [4, 5, 99, 7]], np.int32)  # row 32.. of seq 1: bad page
+    kpool = torch.zeros((num_pages, page_rows, H, D), dtype=torch.bfloat16, device="cuda")
+    vpool = torch.zeros_like(kpool)
+    q = dev(randn_u16((B, H, D), 790))
+    out = torch.empty((B, H * D), dtype=torch.bfloat16, device="cuda")
+    ws = torch.zeros(nc.decode_workspace_bytes(B, 64, H), dtype=torch.uint8, device="cuda")
+    nc.device_status(reset=True)
+    nc.decode_attention_paged(out, q, q, q, kpool, vpool,
+                              torch.tensor(table, device="cuda"),
+                              torch.tensor(lens, dtype=torch.int32, device="cuda"), H, SCALE,
+                              64, ws)
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) & 0x400
+    # only the two appended rows were written: row 39 of seq 0 (page 2), row 49 of seq 1 (page 7)
+    for pg in (0, 1, 3, 4, 5, 6):
+        assert int(kpool[pg].count_nonzero()) == 0 and int(vpool[pg].count_nonzero()) == 0
+    assert int(kpool[2, 39 % 16].count_nonzero()) > 0 and int(kpool[7, 49 % 16].count_nonzero()) > 0
+
+
 def test_decode_overlap_after_qkv_gemm(nc):
     """nc_decode_attention_overlap right after the fused Q/K/V GEMM that produces its q, k_new
     and v_new (the engine's order): the attention CTAs load cache rows while the GEMM runs and
