@@ -19,9 +19,10 @@ What runs where:
   per-row scale applied inside them.  A decode layer is four GEMM launches and one attention
   launch; the step starts with one embedding-gather + RMSNorm launch and ends with an argmax
   launch on the device (gemm.py);
-* the prompt pass's GEMMs (one sequence of P rows at a time) on cuBLAS through torch (fp32
-  accumulation; product + residual rounded once), with the parameter-free RMSNorm, ReLU^2, tanh
-  cap and embedding gather as torch operations there.
+* the prompt pass (all sequences' B*P rows together; `admit` runs one sequence) with its GEMMs
+  on cuBLAS through torch (fp32 accumulation; product + residual rounded once) and the
+  parameter-free RMSNorm, ReLU^2, tanh cap and embedding gather as torch operations, its
+  attention on this library (RoPE/QK-norm/append pass and the batched tcgen05 prefill).
 
 A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
 and replayed; the device length array advances inside the graph.  The reference engine runs one
@@ -139,12 +140,31 @@ class BatchedEngine:
 
     def prefill(self, prompts):
         """prompts: int64 [B, P] token ids; fills the caches of every slot and sets the first
-        generated token of every sequence (returned, and kept as the next decode input)."""
+        generated token of every sequence (returned, and kept as the next decode input).
+        All B sequences go through each layer together: the GEMMs run on B*P rows, the RoPE +
+        QK-norm + append pass writes each slot's cache rows [0, P), and one batched prefill
+        attention launch covers every sequence."""
         B, P = prompts.shape
         assert B == self.B and P < self.max_len
-        first = torch.empty(B, dtype=torch.int64, device=prompts.device)
-        for b in range(B):
-            first[b] = self._prompt_pass(b, prompts[b])
+        w = self.w
+        x = rmsnorm(w.embed[prompts.reshape(-1)])  # [B*P, N_EMBD]
+        offs = torch.zeros(B, dtype=torch.int32, device=prompts.device)
+        stride = self.max_len * N_HEAD * HEAD_DIM
+        for i, l in enumerate(w.layers):
+            xn = rmsnorm(x)
+            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
+            for b in range(B):
+                r = slice(b * P, (b + 1) * P)
+                attn.rope_qknorm_append(q[r], k[r], v[r], self.k[i][b], self.v[i][b], P, N_HEAD,
+                                        0)
+            a = torch.empty_like(q)
+            attn.prefill_attention_batched(a, q, self.k[i], self.v[i], stride, self.max_len, offs,
+                                           P, N_HEAD, SCALE)
+            x = torch.addmm(x, a, l["o"].t())
+            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
+            x = torch.addmm(x, h, l["down"].t())
+        last = x.view(B, P, N_EMBD)[:, -1]
+        first = torch.argmax(logits_of(w, last).float(), dim=-1)
         self.kv_len.fill_(P)
         self.tok.copy_(first)
         self.active.fill_(1)
