@@ -164,6 +164,27 @@ int nc_prefill_attention_batched(void* out, const void* q, const void* k_slab,
                                  const int* kv_offset, int batch, int seq_q, int heads,
                                  float scale, cudaStream_t stream);
 
+/* Paged forms of the prompt path, for caches kept in pages (see nc_decode_attention_paged):
+ * pools [num_pages][page_rows][heads][128] bf16.
+ *
+ * nc_rope_qknorm_append_paged: as nc_rope_qknorm_append for one sequence whose cache rows are
+ * the pages pages[0..n_pages) (a HOST array of page ids, in position order): position p goes
+ * to row p % page_rows of page pages[p / page_rows].  Every page id the chunk
+ * [start_pos, start_pos + seq_len) touches is checked on the host (NC_ERR_INVALID_ARG).
+ *
+ * nc_prefill_attention_paged: as nc_prefill_attention_batched with the keys and values read
+ * through a device page table [batch][pages_per_seq] (page_rows a multiple of 128, so that one
+ * 128-key block lies in one page).  A key block past the table row or a page id outside
+ * [0, num_pages) is read as zeros and sets bit 0x400 of the device status word. */
+int nc_rope_qknorm_append_paged(void* q, const void* k, const void* v, void* k_pool,
+                                void* v_pool, int num_pages, int page_rows, const int* pages,
+                                int n_pages, int seq_len, int heads, int start_pos,
+                                cudaStream_t stream);
+int nc_prefill_attention_paged(void* out, const void* q, const void* k_pool, const void* v_pool,
+                               int num_pages, int page_rows, const int* page_table,
+                               int pages_per_seq, const int* kv_offset, int batch, int seq_q,
+                               int heads, float scale, cudaStream_t stream);
+
 /* ----------------------------------------------------------------------------------------
  * KV cache.  One slab per layer and per K/V: [n_seqs][max_len][heads][128] bf16, allocated
  * once at full length and zero-filled (no grow-and-copy), with per-sequence lengths tracked

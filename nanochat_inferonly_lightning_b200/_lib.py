@@ -44,6 +44,12 @@ SIGNATURES = {
     "nc_prefill_attention_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
                                              c_longlong, c_int, c_void_p, c_int, c_int, c_int,
                                              c_float, c_void_p]),
+    "nc_rope_qknorm_append_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_int, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                                            c_void_p]),
+    "nc_prefill_attention_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                           c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                           c_float, c_void_p]),
     "nc_kv_cache_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_int]),
     "nc_kv_cache_destroy": (c_int, [c_void_p]),
     "nc_kv_cache_k": (c_void_p, [c_void_p, c_int, c_int]),

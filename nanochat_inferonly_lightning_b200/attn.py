@@ -130,6 +130,36 @@ def decode_attention_paged(out, q, k_new, v_new, k_pool, v_pool, page_table, kv_
                                              _stream(stream)))
 
 
+def rope_qknorm_append_paged(q, k, v, k_pool, v_pool, pages, seq_len, heads, start_pos,
+                             stream=None):
+    """nc_rope_qknorm_append_paged: q gets RoPE + QK-norm in place; k (after RoPE + QK-norm) and
+    v land at positions start_pos.. of the sequence whose pages are `pages` (host list of page
+    ids, in position order) in the pools [num_pages, page_rows, heads, 128]."""
+    _bf16(q, k, v, k_pool, v_pool)
+    ids = (ctypes.c_int * len(pages))(*[int(x) for x in pages])
+    lib = _lib.load()
+    _lib.check("nc_rope_qknorm_append_paged",
+               lib.nc_rope_qknorm_append_paged(_ptr(q), _ptr(k), _ptr(v), _ptr(k_pool),
+                                               _ptr(v_pool), int(k_pool.shape[0]),
+                                               int(k_pool.shape[1]), ids, len(pages), seq_len,
+                                               heads, start_pos, _stream(stream)))
+
+
+def prefill_attention_paged(out, q, k_pool, v_pool, page_table, kv_offset, seq_q, heads, scale,
+                            stream=None):
+    """nc_prefill_attention_paged: causal chunked prefill of q [B, seq_q, heads, 128] over keys
+    read through page_table (int32 CUDA [B, pages_per_seq]); kv_offset int32 CUDA [B]."""
+    _bf16(out, q, k_pool, v_pool)
+    batch = int(kv_offset.numel())
+    lib = _lib.load()
+    _lib.check("nc_prefill_attention_paged",
+               lib.nc_prefill_attention_paged(_ptr(out), _ptr(q), _ptr(k_pool), _ptr(v_pool),
+                                              int(k_pool.shape[0]), int(k_pool.shape[1]),
+                                              _ptr(page_table), int(page_table.shape[1]),
+                                              _ptr(kv_offset), batch, seq_q, heads, float(scale),
+                                              _stream(stream)))
+
+
 def prefill_attention_batched(out, q, k_slab, v_slab, seq_stride, rows_per_seq, kv_offset,
                               seq_q, heads, scale, stream=None):
     """Batched chunked prefill over caches that are slices of one slab (seq_stride elements

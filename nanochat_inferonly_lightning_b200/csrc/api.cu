@@ -420,6 +420,79 @@ int nc_decode_attention_overlap(void* out, const void* q, const void* k_new, con
                          workspace_bytes, stream, 1);
 }
 
+int nc_prefill_attention_paged(void* out, const void* q, const void* k_pool, const void* v_pool,
+                               int num_pages, int page_rows, const int* page_table,
+                               int pages_per_seq, const int* kv_offset, int batch, int seq_q,
+                               int heads, float scale, cudaStream_t stream) {
+    if (batch < 0 || seq_q < 0 || check_heads(heads)) return NC_ERR_INVALID_ARG;
+    if (batch == 0 || seq_q == 0) return NC_OK;
+    if (!out || !q || !k_pool || !v_pool || !page_table || !kv_offset) return NC_ERR_INVALID_ARG;
+    if (page_rows < 128 || page_rows % 128 || num_pages < 1 || pages_per_seq < 1 ||
+        (long long)num_pages * page_rows > INT32_MAX / 2)
+        return NC_ERR_INVALID_ARG;
+    if (!aligned16(out) || !aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool))
+        return NC_ERR_MISALIGNED;
+    PrefillArgs a{};
+    a.out = static_cast<bf16*>(out);
+    a.q = static_cast<const bf16*>(q);
+    a.k = static_cast<const bf16*>(k_pool);
+    a.v = static_cast<const bf16*>(v_pool);
+    a.kv_rows = num_pages * page_rows;
+    a.kv_offset_dev = kv_offset;
+    a.batch = batch;
+    a.seq_q = seq_q;
+    a.heads = heads;
+    a.scale = scale;
+    a.page_table = page_table;
+    a.page_rows = page_rows;
+    a.pages_per_seq = pages_per_seq;
+    a.num_pages = num_pages;
+    int st = status_word(&a.status);
+    if (st) return st;
+    cudaError_t e = launch_prefill(a, stream);
+    return e == cudaSuccess ? NC_OK : cuda_fail(e);
+}
+
+int nc_rope_qknorm_append_paged(void* q, const void* k, const void* v, void* k_pool,
+                                void* v_pool, int num_pages, int page_rows, const int* pages,
+                                int n_pages, int seq_len, int heads, int start_pos,
+                                cudaStream_t stream) {
+    if (seq_len < 0 || start_pos < 0 || check_heads(heads)) return NC_ERR_INVALID_ARG;
+    if (seq_len == 0) return NC_OK;
+    if (!q || !k || !v || !k_pool || !v_pool || !pages || page_rows < 1 || num_pages < 1)
+        return NC_ERR_INVALID_ARG;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_pool) ||
+        !aligned16(v_pool))
+        return NC_ERR_MISALIGNED;
+    if ((long long)start_pos + seq_len > kRopeMaxSeq) return NC_ERR_RANGE;
+    if ((long long)(start_pos + seq_len - 1) / page_rows >= n_pages) return NC_ERR_INVALID_ARG;
+    for (int j = start_pos / page_rows; j <= (start_pos + seq_len - 1) / page_rows; ++j)
+        if (pages[j] < 0 || pages[j] >= num_pages) return NC_ERR_INVALID_ARG;
+    RopeArgs a{};
+    int st = ensure_rope(&a.rope_cs);
+    if (st) return st;
+    const size_t rowstride = (size_t)heads * kHeadDim;
+    // One launch per page the chunk touches; each page is contiguous in the pool.
+    for (int p0 = start_pos; p0 < start_pos + seq_len;) {
+        const int j = p0 / page_rows;
+        const int p1 = std::min(start_pos + seq_len, (j + 1) * page_rows);
+        const size_t src = (size_t)(p0 - start_pos) * rowstride;
+        const size_t dst = ((size_t)pages[j] * page_rows + (p0 - j * page_rows)) * rowstride;
+        a.q = static_cast<bf16*>(q) + src;
+        a.k = static_cast<const bf16*>(k) + src;
+        a.v = static_cast<const bf16*>(v) + src;
+        a.k_dst = static_cast<bf16*>(k_pool) + dst;
+        a.v_dst = static_cast<bf16*>(v_pool) + dst;
+        a.seq_len = p1 - p0;
+        a.heads = heads;
+        a.start_pos = p0;
+        cudaError_t e = launch_rope(kRopeNormAppend, a, stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+        p0 = p1;
+    }
+    return NC_OK;
+}
+
 int nc_prefill_attention_batched(void* out, const void* q, const void* k_slab,
                                  const void* v_slab, long long seq_stride, int rows_per_seq,
                                  const int* kv_offset, int batch, int seq_q, int heads,

@@ -261,6 +261,13 @@ struct PrefillArgs {
     int heads;
     float scale;
     int* status;                  // device status word for bounded waits
+    // Paged cache (page_table != null): k / v are pools [num_pages][page_rows][heads][128],
+    // page_rows a multiple of 128, and key row r of sequence b is row r % page_rows of page
+    // page_table[b * pages_per_seq + r / page_rows].
+    const int* page_table;
+    int page_rows;
+    int pages_per_seq;
+    int num_pages;
 };
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);

@@ -105,6 +105,8 @@ struct PrefillKParams {
     int total_tiles;
     float scale_log2;
     int* status;
+    const int* page_table;  // paged K/V (see PrefillArgs); null: per-sequence caches
+    int page_rows, pages_per_seq, num_pages;
 };
 
 // One tile of work: its coordinates and how many key blocks it visits.
@@ -276,6 +278,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < t.nb; ++j, ++g) {
                     const int st = g & 1;
                     const uint32_t ph = ((g >> 1) - 1) & 1;  // previous use of stage st
+                    // Key block j: rows [j*128, j*128 + 128) of sequence t.b, or, paged, of its
+                    // page (a page holds a multiple of 128 rows).  The page id is read before
+                    // the ring wait below so that its latency overlaps the wait.  A block past
+                    // the sequence's pages or a page id outside the pool is flagged and loaded
+                    // from an out-of-range row (TMA fills it with zeros).
+                    int ky = j * kBN, kz = t.b;
+                    if (p.page_table) {
+                        const int pidx = (j * kBN) / p.page_rows;
+                        const int page = pidx < p.pages_per_seq
+                                             ? p.page_table[t.b * p.pages_per_seq + pidx]
+                                             : -1;
+                        kz = 0;
+                        if (page < 0 || page >= p.num_pages) {
+                            atomicOr(p.status, kStatusBounds);
+                            ky = -kBN;
+                        } else {
+                            ky = page * p.page_rows + (j * kBN) % p.page_rows;
+                        }
+                    }
                     // K stage st is free once QK(g-2) completed (kBarS), V stage once PV(g-2) did.
                     if (g >= 2 && !(ok = mbar_wait(&bars[(kq ? kBarS : kBarPV) + st], ph, abort_flag,
                                                    p.status, kq ? 2 : 3)))
@@ -284,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint64_t* full = &bars[(kq ? kBarKFull : kBarVFull) + st];
                     const CUtensorMap* map = kq ? &tmK : &tmV;
                     mbar_arrive_expect_tx(full, kTileBytes);
-                    tma_load_3d(dst, map, full, x0, j * kBN, t.b);
-                    tma_load_3d(dst + kBoxBytes, map, full, x0 + 64, j * kBN, t.b);
+                    tma_load_3d(dst, map, full, x0, ky, kz);
+                    tma_load_3d(dst + kBoxBytes, map, full, x0 + 64, ky, kz);
                 }
                 ++qi;
             }
@@ -768,9 +789,15 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     const long long qo_stride = (long long)a.seq_q * a.heads * 128;
     // Q/K/V loads move (64 dims x 128 rows) boxes; the output is stored by each softmax warp
     // in (64 dims x 32 rows) boxes.
+    // Paged K/V: one map over the whole pool (batch extent 1); the producer turns (sequence,
+    // key block) into a pool row through the page table.
+    const bool paged = a.page_table != nullptr;
+    const int kv_map_rows = paged ? a.num_pages * a.page_rows : kv_rows;
+    const int kv_map_batch = paged ? 1 : a.batch;
+    const long long kv_map_stride = paged ? 0 : a.kv_batch_stride;
     if (!cached_map(&mq, a.q, a.heads, a.seq_q, a.batch, qo_stride, dev, 128) ||
-        !cached_map(&mk, a.k, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev, 128) ||
-        !cached_map(&mv, a.v, a.heads, kv_rows, a.batch, a.kv_batch_stride, dev, 128) ||
+        !cached_map(&mk, a.k, a.heads, kv_map_rows, kv_map_batch, kv_map_stride, dev, 128) ||
+        !cached_map(&mv, a.v, a.heads, kv_map_rows, kv_map_batch, kv_map_stride, dev, 128) ||
         !cached_map(&mo, a.out, a.heads, a.seq_q, a.batch, qo_stride, dev, 32))
         return cudaErrorInvalidValue;
     PrefillKParams kp;
@@ -791,6 +818,10 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     kp.total_tiles = kp.n_qtiles * a.heads * a.batch;
     kp.scale_log2 = a.scale * kLog2e;
     kp.status = a.status;
+    kp.page_table = a.page_table;
+    kp.page_rows = a.page_rows;
+    kp.pages_per_seq = a.pages_per_seq;
+    kp.num_pages = a.num_pages;
     // Persistent: one CTA per SM (or fewer when there are fewer tiles).
     const unsigned grid = (unsigned)std::min<long long>(kp.total_tiles, sm_count[dev]);
     cudaLaunchConfig_t cfg = {};

@@ -428,6 +428,56 @@ def test_prefill_batched(nc, B, chunk, off, rows):
     assert_close_bf16(bf16_to_u16(out), want, what="batched prefill")
 
 
+@pytest.mark.parametrize("offs,chunk,page_rows", [([0, 200, 700], 300, 128),
+                                                   ([1536, 0], 512, 256)])
+def test_prefill_paged(nc, offs, chunk, page_rows):
+    """Chunked prefill over a paged cache: nc_rope_qknorm_append_paged writes each sequence's
+    chunk into its (shuffled) pages, crossing page edges; nc_prefill_attention_paged then reads
+    the keys through the page table.  Against the oracle on the equivalent contiguous caches."""
+    B = len(offs)
+    pps = -(-max(o + chunk for o in offs) // page_rows)
+    num_pages = B * pps + 2
+    rng = np.random.default_rng(800 + page_rows)
+    perm = rng.permutation(num_pages).astype(np.int32)
+    table = perm[:B * pps].reshape(B, pps)
+    kpool = np.zeros((num_pages, page_rows, H, D), np.uint16)
+    vpool = np.zeros_like(kpool)
+    qs, ks, vs, wants, wks, wvs, wqs = [], [], [], [], [], [], []
+    for b, off in enumerate(offs):
+        kc = np.zeros((pps * page_rows, H, D), np.uint16)
+        vc = np.zeros_like(kc)
+        if off:
+            kc[:off] = normed(randn_u16((off, H, D), 810 + b), 0)
+            vc[:off] = randn_u16((off, H, D), 820 + b)
+        q, k, v = (randn_u16((chunk, H, D), 830 + 3 * b + i) for i in range(3))
+        wq, wkc, wvc = oracle.rope_qknorm_append(q, k, v, kc, vc, chunk, H, off)
+        wants.append(oracle.flash_attention(wq, wkc, wvc, chunk, off + chunk, H, SCALE, off))
+        for j in range(pps):
+            kpool[table[b, j]] = kc[j * page_rows:(j + 1) * page_rows]
+            vpool[table[b, j]] = vc[j * page_rows:(j + 1) * page_rows]
+        qs.append(q), ks.append(k), vs.append(v), wks.append(wkc), wvs.append(wvc), wqs.append(wq)
+    tk, tv = dev(kpool), dev(vpool)
+    tq = dev(np.stack(qs))
+    for b, off in enumerate(offs):
+        nc.rope_qknorm_append_paged(tq[b], dev(ks[b]), dev(vs[b]), tk, tv, list(table[b]), chunk,
+                                    H, off)
+    out = torch.empty((B, chunk, H * D), dtype=torch.bfloat16, device="cuda")
+    nc.prefill_attention_paged(out, tq, tk, tv, torch.tensor(table, device="cuda"),
+                               torch.tensor(offs, dtype=torch.int32, device="cuda"), chunk, H,
+                               SCALE)
+    torch.cuda.synchronize()
+    gk, gv = bf16_to_u16(tk), bf16_to_u16(tv)
+    for b, off in enumerate(offs):
+        assert ulp_diff_bf16(bf16_to_u16(tq[b]), wqs[b]).max() <= 1
+        rows = np.arange(off, off + chunk)
+        got_k = gk[table[b, rows // page_rows], rows % page_rows]
+        got_v = gv[table[b, rows // page_rows], rows % page_rows]
+        assert ulp_diff_bf16(got_k, wks[b][off:off + chunk]).max() <= 1
+        assert np.array_equal(got_v, wvs[b][off:off + chunk])
+        assert_close_bf16(bf16_to_u16(out[b]), wants[b], what=f"paged prefill seq {b}")
+    assert nc.device_status(reset=True) == 0
+
+
 # ----------------------------------------------------------------------------- KV cache object
 def test_kv_cache_prefill_then_decode(nc):
     """Prefill a prompt through the cache object, then decode steps for two sequences; the
