@@ -498,12 +498,31 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     const int H = a.heads;
     const size_t rowstride = (size_t)H * kHeadDim;
     const size_t qoff = (size_t)b * rowstride + (size_t)h * kHeadDim + 8 * sub;
-    // The sequence's length and cache bases first, then this split's cache rows: none of them
-    // is written by the kernel that precedes an overlapped launch (a.overlap), so they are
-    // read before griddepcontrol.wait; the query and the new key and value come after it.
-    const int Lraw = raw_len(a, b);
-    const int L = min(Lraw, a.max_kv_len);
+    // The sequence's length and this warp's cache base (or page id) first, loaded together,
+    // then this split's cache rows: none of them is written by the kernel that precedes an
+    // overlapped launch (a.overlap), so they are read before griddepcontrol.wait; the query
+    // and the new key and value come after it.
     const int T = a.split_len;
+    // This warp's rows start at w0 (half-warp `half` takes w0 + half, w0 + half + 2, ...); the
+    // 16 rows are consecutive in the cache (a paged cache's pages hold a multiple of 16 rows,
+    // and w0 is a multiple of 16), so one base or page id per warp.
+    const int w0 = split * T + 16 * warp;
+    const int Lraw = raw_len(a, b);
+    // Without an overlapped launch the query has no producer still running: load it with the
+    // rest, so that its RoPE + QK-norm overlaps the cache loads.
+    uint4 qr = make_uint4(0u, 0u, 0u, 0u);
+    if (!a.overlap) qr = *reinterpret_cast<const uint4*>(a.q + qoff);
+    const bf16* kbase = nullptr;
+    const bf16* vbase = nullptr;
+    int page = 0;
+    if (PAGED) {
+        const int pidx = w0 / a.page_rows;
+        page = pidx < a.pages_per_seq ? a.page_table[(size_t)b * a.pages_per_seq + pidx] : -1;
+    } else {
+        kbase = a.k_cache ? a.k_cache[b] : a.k_single;
+        vbase = a.v_cache ? a.v_cache[b] : a.v_single;
+    }
+    const int L = min(Lraw, a.max_kv_len);
     const int n_splits = L > 0 ? (L + T - 1) / T : 1;
     if (split >= n_splits) return;  // uniform across the CTA
     if (split == 0 && h == 0 && threadIdx.x == 0 && Lraw > a.max_kv_len)
@@ -522,13 +541,21 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
     const bool owns_new = a.k_new != nullptr && ke == L;
     const int ke_s = owns_new ? ke - 1 : ke;  // the new key comes from registers
 
-    // This warp's rows [w0, w1); half-warp `half` takes w0 + half, w0 + half + 2, ...
-    const int w0 = ks + 16 * warp;
-    const int w1 = min(ke_s, w0 + 16);
-    // The warp's 16 rows are consecutive in the cache (a paged cache's pages hold a multiple
-    // of 16 rows, and w0 is a multiple of 16): one base per warp.
-    const bf16* kb = w0 < w1 ? kv_row<PAGED>(a, false, b, w0) : nullptr;
-    const bf16* vb = w0 < w1 ? kv_row<PAGED>(a, true, b, w0) : nullptr;
+    const int w1 = min(ke_s, w0 + 16);  // this warp's rows are [w0, w1)
+    const bf16* kb = nullptr;
+    const bf16* vb = nullptr;
+    if (w0 < w1) {
+        if (!PAGED) {
+            kb = kbase + (size_t)w0 * rowstride;
+            vb = vbase + (size_t)w0 * rowstride;
+        } else if (page >= 0 && page < a.num_pages) {
+            const size_t prow = (size_t)page * a.page_rows + (w0 % a.page_rows);
+            kb = a.k_pool + prow * rowstride;
+            vb = a.v_pool + prow * rowstride;
+        } else {
+            atomicOr(a.status, kStatusBounds);
+        }
+    }
     uint4 kr[8], vr[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -542,7 +569,7 @@ __global__ void __launch_bounds__(128) decode_head_kernel(DecodeArgs a) {
         }
     }
     griddep_wait();  // no-op unless launched as a programmatic dependent launch
-    const uint4 qr = *reinterpret_cast<const uint4*>(a.q + qoff);
+    if (a.overlap) qr = *reinterpret_cast<const uint4*>(a.q + qoff);
     float qf[8];
     {
         if (a.q_raw) {
