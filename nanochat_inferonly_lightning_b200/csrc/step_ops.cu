@@ -170,6 +170,34 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
     return base + x - v;
 }
 
+// Exclusive prefix sum of one float per thread over the block (1024 threads); *total gets the
+// sum.  Same structure as block_exclusive_scan.
+__device__ float block_exclusive_scan_f(float v, float* warp_sums, float* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        float w = warp_sums[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const float base = warp > 0 ? warp_sums[warp - 1] : 0.f;
+    *total = warp_sums[31];
+    __syncthreads();
+    return base + x - v;
+}
+
 struct SampleSmem {
     unsigned long long cand[kSampleMaxK];  // (key << 32) | (0xFFFFFFFF - index)
     float q[kSampleMaxK];                  // normalised probability of each candidate
@@ -177,6 +205,7 @@ struct SampleSmem {
     int warp_sums[32];
     float fred[32];
     int b1, above1, kstar, c_gt;
+    int found;
 };
 
 __global__ void __launch_bounds__(kSampleThreads)
@@ -220,6 +249,47 @@ __global__ void __launch_bounds__(kSampleThreads)
     __syncthreads();
     sum = 0.f;
     for (int w = 0; w < 32; ++w) sum += sm.fred[w];
+    if (top_k <= 0) {
+        // No filter (top_k_filter and top_p_filter return at once, :62-73): the entries stay
+        // in index order; renormalise (:116-119) and take the first index whose running sum
+        // exceeds r (:121-128), else the last index.  The running sum is a block-wide prefix
+        // sum over the threads' index-ordered slices, each slice summed in order.
+        __syncthreads();  // every thread has read sm.fred (the softmax denominator) above
+        float s2 = 0.f;
+        for (int c = c0; c < c1; c += 8) {
+            float f[8];
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s2 += expf((f[e] - mx) / temperature) / sum;
+        }
+        float tot;
+        block_exclusive_scan_f(s2, sm.fred, &tot);  // tot = sum of the normalised entries
+        const float s2all = tot;
+        float part = 0.f;
+        for (int c = c0; c < c1; c += 8) {
+            float f[8];
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part += expf((f[e] - mx) / temperature) / sum / s2all;
+        }
+        const float base = block_exclusive_scan_f(part, sm.fred, &tot);
+        if (tid == 0) sm.found = vocab - 1;
+        __syncthreads();
+        const float r = uniforms[blockIdx.x];
+        if (c0 < c1 && base <= r && r < base + part) {
+            float cs = base;
+            for (int c = c0; c < c1; ++c) {
+                cs += expf((__bfloat162float(row[c]) - mx) / temperature) / sum / s2all;
+                if (r < cs) {
+                    atomicMin(&sm.found, c);
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0) out[blockIdx.x] = sm.found;
+        return;
+    }
     for (int c = c0; c < c1; c += 8) {
         const uint4 v = *reinterpret_cast<const uint4*>(row + c);
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
@@ -393,8 +463,13 @@ int nc_sample_rows(int* out, const void* logits, int rows, int vocab, float temp
     if (!out || !logits) return NC_ERR_INVALID_ARG;
     if (reinterpret_cast<uintptr_t>(logits) & 15) return NC_ERR_MISALIGNED;
     if (temperature == 0.f) return nc_argmax_rows(out, logits, rows, vocab, stream);
-    if (top_k < 1 || top_k > kSampleMaxK || top_k >= vocab || !(top_p > 0.f) || !uniforms)
-        return NC_ERR_INVALID_ARG;
+    if (!(top_p > 0.f) || !uniforms) return NC_ERR_INVALID_ARG;
+    // top_k <= 0 or >= vocab: no top-k filter.  Then top_p must be off (>= 1): a top-p cut over
+    // the whole vocabulary (a full sort) is not supported.
+    const bool no_topk = top_k <= 0 || top_k >= vocab;
+    if (no_topk && top_p < 1.0f) return NC_ERR_INVALID_ARG;
+    if (!no_topk && top_k > kSampleMaxK) return NC_ERR_INVALID_ARG;
+    if (no_topk) top_k = 0;
     sample_rows_kernel<<<rows, kSampleThreads, 0, stream>>>(
         out, static_cast<const bf16*>(logits), vocab, temperature, top_k, top_p, uniforms);
     cudaError_t e = cudaGetLastError();

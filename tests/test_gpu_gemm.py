@@ -285,7 +285,10 @@ def _sample_margin(row_f32, T, k, p, r):
     lf = row_f32.astype(np.float64)
     pr = np.exp((lf - lf.max()) / T)
     pr /= pr.sum()
-    order = np.lexsort((np.arange(len(pr)), -pr))[:k]
+    if 0 < k < len(pr):
+        order = np.lexsort((np.arange(len(pr)), -pr))[:k]
+    else:  # no top-k filter: index order
+        order = np.arange(len(pr))
     cs = np.cumsum(pr[order])
     m = np.abs(cs - p).min() if p < 1.0 else 1.0
     if p < 1.0 and (cs > p).any():
@@ -324,6 +327,21 @@ def test_sample_rows_against_oracle(G):
                 assert _sample_margin(lf, T, k, p, float(uh[r])) < 1e-4, (T, k, p, r, got[r], want)
                 skipped += 1
     assert skipped <= 3, skipped
+    # top_k off (0, or >= vocab) with top_p off: the whole row in index order.  Its 65536
+    # intervals are ~1.5e-5 wide, as wide as the gap between a sequential and a parallel fp32
+    # running sum, so the draw is checked against exact (fp64) running sums: the chosen index's
+    # interval must lie within 1e-4 of r.
+    for T, k in [(1.0, 0), (0.8, V)]:
+        out = torch.empty(R, dtype=torch.int32, device="cuda")
+        G.sample_rows(out, logits, T, k, 1.0, u)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for r in range(R):
+            lf = oracle.bf16_bits_to_f32(host[r]).astype(np.float64)
+            w = np.exp((lf - lf.max()) / T)
+            cs = np.cumsum(w / w.sum())
+            lo = cs[got[r] - 1] if got[r] > 0 else 0.0
+            assert lo - 1e-4 <= uh[r] <= cs[got[r]] + 1e-4, (T, k, r, got[r])
     # temperature 0 is the greedy path
     out = torch.empty(R, dtype=torch.int32, device="cuda")
     G.sample_rows(out, logits, 0.0, 50, 0.9, None)
