@@ -92,17 +92,7 @@ class BatchedEngine:
             torch.cuda.manual_seed(seed)
         self.uniforms = torch.zeros(batch, dtype=torch.float32, device=device)
         attn.init_rope_tables()
-        shape = (batch, max_len, N_HEAD, HEAD_DIM)
-        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
-        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
-        row = max_len * N_HEAD * HEAD_DIM * 2
-
-        def table(t):
-            return torch.tensor([t.data_ptr() + b * row for b in range(batch)], dtype=torch.int64,
-                                device=device)
-
-        self.k_tab = [table(t) for t in self.k]
-        self.v_tab = [table(t) for t in self.v]
+        self._alloc_caches(device)
         self.kv_len = torch.zeros(batch, dtype=torch.int32, device=device)
         self.ws = torch.zeros(attn.decode_workspace_bytes(batch, max_len, N_HEAD),
                               dtype=torch.uint8, device=device)
@@ -119,6 +109,42 @@ class BatchedEngine:
         self.logits = torch.zeros((batch, VOCAB), **bf)
         self.graph = None
 
+    def _alloc_caches(self, device):
+        """One K and one V slab per layer, [batch, max_len, heads, 128], and device arrays of the
+        per-sequence bases for the batched decode kernel."""
+        shape = (self.B, self.max_len, N_HEAD, HEAD_DIM)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        row = self.max_len * N_HEAD * HEAD_DIM * 2
+
+        def table(t):
+            return torch.tensor([t.data_ptr() + b * row for b in range(self.B)],
+                                dtype=torch.int64, device=device)
+
+        self.k_tab = [table(t) for t in self.k]
+        self.v_tab = [table(t) for t in self.v]
+
+    # ------------------------------------------------------------------ cache access
+    def _prompt_attention(self, i, b, q, k, v, P, a):
+        """Layer i, one sequence in slot b: RoPE + QK-norm + append of its P rows, attention."""
+        attn.rope_qknorm_append(q, k, v, self.k[i][b], self.v[i][b], P, N_HEAD, 0)
+        attn.flash_attention(a, q, self.k[i][b], self.v[i][b], P, P, N_HEAD, SCALE, 0)
+
+    def _prompt_attention_all(self, i, q, k, v, P, a):
+        """Layer i, every slot's prompt of P rows (rows b*P.. of q, k, v)."""
+        for b in range(self.B):
+            r = slice(b * P, (b + 1) * P)
+            attn.rope_qknorm_append(q[r], k[r], v[r], self.k[i][b], self.v[i][b], P, N_HEAD, 0)
+        offs = torch.zeros(self.B, dtype=torch.int32, device=q.device)
+        attn.prefill_attention_batched(a, q, self.k[i], self.v[i], self.max_len * N_HEAD * HEAD_DIM,
+                                       self.max_len, offs, P, N_HEAD, SCALE)
+
+    def _decode_attention(self, i, a, qkv):
+        # right after the Q/K/V GEMM, which writes no cache: the attention CTAs may start
+        # loading cache rows while it finishes
+        attn.decode_attention(a, qkv[0], qkv[1], qkv[2], self.k_tab[i], self.v_tab[i],
+                              self.kv_len, N_HEAD, SCALE, self.max_len, self.ws, overlap=True)
+
     # ------------------------------------------------------------------ prompt
     def _prompt_pass(self, b, prompt):
         """Prompt pass of one sequence into slot b's caches (rows [0, P)); returns its first
@@ -131,8 +157,7 @@ class BatchedEngine:
             xn = rmsnorm(x)
             q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
             a = torch.empty_like(q)
-            attn.rope_qknorm_append(q, k, v, self.k[i][b], self.v[i][b], P, N_HEAD, 0)
-            attn.flash_attention(a, q, self.k[i][b], self.v[i][b], P, P, N_HEAD, SCALE, 0)
+            self._prompt_attention(i, b, q, k, v, P, a)
             x = torch.addmm(x, a, l["o"].t())
             h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
             x = torch.addmm(x, h, l["down"].t())
@@ -148,18 +173,11 @@ class BatchedEngine:
         assert B == self.B and P < self.max_len
         w = self.w
         x = rmsnorm(w.embed[prompts.reshape(-1)])  # [B*P, N_EMBD]
-        offs = torch.zeros(B, dtype=torch.int32, device=prompts.device)
-        stride = self.max_len * N_HEAD * HEAD_DIM
         for i, l in enumerate(w.layers):
             xn = rmsnorm(x)
             q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
-            for b in range(B):
-                r = slice(b * P, (b + 1) * P)
-                attn.rope_qknorm_append(q[r], k[r], v[r], self.k[i][b], self.v[i][b], P, N_HEAD,
-                                        0)
             a = torch.empty_like(q)
-            attn.prefill_attention_batched(a, q, self.k[i], self.v[i], stride, self.max_len, offs,
-                                           P, N_HEAD, SCALE)
+            self._prompt_attention_all(i, q, k, v, P, a)
             x = torch.addmm(x, a, l["o"].t())
             h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
             x = torch.addmm(x, h, l["down"].t())
@@ -196,11 +214,7 @@ class BatchedEngine:
         for i, l in enumerate(w.layers):
             # RMSNorm -> Q/K/V (src/model.cpp:110-116)
             G.gemm_skinny(qkv, x, self.wqkv[i], flags=G.NORM_INPUT, seg_cols=N_EMBD)
-            # right after the Q/K/V GEMM, which writes no cache: the attention CTAs may start
-            # loading cache rows while it finishes
-            attn.decode_attention(a, qkv[0], qkv[1], qkv[2], self.k_tab[i], self.v_tab[i],
-                                  self.kv_len, N_HEAD, SCALE, self.max_len, self.ws,
-                                  overlap=True)
+            self._decode_attention(i, a, qkv)
             G.gemm_skinny(x, a, l["o"], residual=x)                      # :139
             G.gemm_skinny(h, x, l["up"], flags=G.NORM_INPUT | G.RELU2)  # :146-150
             G.gemm_skinny(x, h, l["down"], residual=x)                   # :153
@@ -231,3 +245,109 @@ class BatchedEngine:
         else:
             self._decode_body()
         return self.tok
+
+
+class PagedEngine(BatchedEngine):
+    """BatchedEngine over a paged KV cache: per layer one K and one V pool of `num_pages` pages of
+    `page_rows` rows (a multiple of 128), shared by all slots, and one device page table
+    [batch, pages_per_seq] used by every layer.  A host-side allocator hands a slot the pages
+    its prompt needs when it is admitted, one more page whenever a decode step is about to write
+    the first row of a new page, and takes them all back when the slot retires, so the cache
+    holds only the live sequences' rows (num_pages may be far below batch * max_len /
+    page_rows).  The attention calls are the library's paged forms (nc_rope_qknorm_append_paged,
+    nc_prefill_attention_paged, nc_decode_attention_paged); everything else is BatchedEngine's.
+    A retired slot's length is set to 0, so a decode step reads and writes none of its old pages.
+    """
+
+    def __init__(self, weights, batch, max_len, page_rows=128, num_pages=None, **kw):
+        assert page_rows % 128 == 0
+        self.page_rows = page_rows
+        self.pages_per_seq = -(-max_len // page_rows)
+        self.num_pages = num_pages or batch * self.pages_per_seq
+        super().__init__(weights, batch, max_len, **kw)
+
+    def _alloc_caches(self, device):
+        shape = (self.num_pages, self.page_rows, N_HEAD, HEAD_DIM)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(N_LAYER)]
+        self.page_table = torch.full((self.B, self.pages_per_seq), -1, dtype=torch.int32,
+                                     device=device)
+        self.free_pages = list(range(self.num_pages - 1, -1, -1))
+        self.pages = [[] for _ in range(self.B)]   # page ids of each slot, in position order
+        self.host_len = [0] * self.B               # rows written per slot (host mirror)
+
+    # ------------------------------------------------------------------ page allocator
+    def _map_rows(self, slot, n_rows):
+        """Makes sure slot's pages cover rows [0, n_rows)."""
+        while len(self.pages[slot]) * self.page_rows < n_rows:
+            if not self.free_pages:
+                raise RuntimeError("paged KV cache: out of pages")
+            pid = self.free_pages.pop()
+            self.page_table[slot, len(self.pages[slot])] = pid
+            self.pages[slot].append(pid)
+
+    def _release(self, slot):
+        self.free_pages.extend(reversed(self.pages[slot]))
+        self.pages[slot] = []
+        self.page_table[slot].fill_(-1)
+
+    def pages_in_use(self):
+        return self.num_pages - len(self.free_pages)
+
+    # ------------------------------------------------------------------ cache access
+    def _prompt_attention(self, i, b, q, k, v, P, a):
+        attn.rope_qknorm_append_paged(q, k, v, self.k[i], self.v[i], self.pages[b], P, N_HEAD, 0)
+        offs = torch.zeros(1, dtype=torch.int32, device=q.device)
+        attn.prefill_attention_paged(a, q, self.k[i], self.v[i], self.page_table[b:b + 1], offs,
+                                     P, N_HEAD, SCALE)
+
+    def _prompt_attention_all(self, i, q, k, v, P, a):
+        for b in range(self.B):
+            r = slice(b * P, (b + 1) * P)
+            attn.rope_qknorm_append_paged(q[r], k[r], v[r], self.k[i], self.v[i], self.pages[b],
+                                          P, N_HEAD, 0)
+        offs = torch.zeros(self.B, dtype=torch.int32, device=q.device)
+        attn.prefill_attention_paged(a, q, self.k[i], self.v[i], self.page_table, offs, P,
+                                     N_HEAD, SCALE)
+
+    def _decode_attention(self, i, a, qkv):
+        attn.decode_attention_paged(a, qkv[0], qkv[1], qkv[2], self.k[i], self.v[i],
+                                    self.page_table, self.kv_len, N_HEAD, SCALE, self.max_len,
+                                    self.ws)
+
+    # ------------------------------------------------------------------ slots and steps
+    def prefill(self, prompts):
+        B, P = prompts.shape
+        for b in range(B):
+            self._release(b)
+            self._map_rows(b, P)
+            self.host_len[b] = P
+        return super().prefill(prompts)
+
+    def admit(self, slot, prompt):
+        P = int(prompt.numel())
+        self._release(slot)
+        self._map_rows(slot, P)
+        self.host_len[slot] = P
+        return super().admit(slot, prompt)
+
+    def retire(self, slot):
+        super().retire(slot)
+        self.kv_len[slot] = 0  # no decode step touches the slot's (released) pages
+        self.host_len[slot] = 0
+        self._release(slot)
+
+    def _before_step(self):
+        """Maps the page each live slot's next row falls in, then advances the host mirror."""
+        for b in range(self.B):
+            if self.pages[b]:  # live slot
+                self._map_rows(b, self.host_len[b] + 1)
+                self.host_len[b] += 1
+
+    def capture(self):
+        self._before_step()  # capture() runs one eager step first
+        return super().capture()
+
+    def step(self):
+        self._before_step()
+        return super().step()

@@ -143,3 +143,33 @@ def test_continuous_batching(setup):
 
     assert slot2 == alone(2, len(slot2))
     assert slot0 == alone(0, len(slot0))
+
+
+def test_paged_engine_matches_contiguous(setup):
+    """PagedEngine (pages of 128 rows from a shared pool, a host allocator, the library's paged
+    prefill / append / decode) gives the contiguous engine's tokens and logits exactly: prompts
+    of 120 tokens, then steps that cross into each sequence's second page.  A retired slot's
+    pages go back to the pool and a sequence admitted there gets fresh ones."""
+    nc, E, w, _ = setup
+    g = torch.Generator().manual_seed(9)
+    P, max_len, steps = 120, 256, 12
+    prompts = torch.randint(2, E.VOCAB, (B, P), generator=g).cuda()
+    ref = E.BatchedEngine(w, B, max_len)
+    pg = E.PagedEngine(w, B, max_len, page_rows=128)
+    assert torch.equal(ref.prefill(prompts), pg.prefill(prompts))
+    assert pg.pages_in_use() == B
+    assert torch.equal(ref.capture(), pg.capture())
+    for _ in range(steps):
+        assert torch.equal(ref.step(), pg.step())
+        assert torch.equal(ref.logits, pg.logits)
+    assert pg.pages_in_use() == 2 * B  # rows 0..132: two pages per sequence
+    # retire slot 1 and admit a new sequence there in both engines
+    ref.retire(1), pg.retire(1)
+    assert pg.pages_in_use() == 2 * B - 2
+    newp = torch.randint(2, E.VOCAB, (P,), generator=g).cuda()
+    assert int(ref.admit(1, newp)) == int(pg.admit(1, newp))
+    for _ in range(3):
+        a, b = ref.step().clone(), pg.step().clone()
+        for s in (0, 1, 2, 3):
+            assert int(a[s]) == int(b[s]), s
+    assert pg.pages_in_use() == 2 * (B - 1) + 1
