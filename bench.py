@@ -139,10 +139,14 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index):
+    def __init__(self, device_index, log_dir=None):
         self.idx = device_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{device_index}.csv")
+        if log_dir is None:
+            import tempfile
+
+            log_dir = tempfile.gettempdir()
+        self.path = os.path.join(log_dir, f"nc_bench_clocks_rank{device_index}.csv")
 
     def start(self):
         try:
@@ -407,21 +411,20 @@ def bench_prefill_e2e(impl, dist, K, Wm, q0, k0, v0):
 
 
 def build_decode_batch(impl, lens, seed):
-    """Per-sequence caches [L_i, 17, 128] (rows 0..L_i-2 filled, normalised), plus the new
-    token's q/k/v [B, 17, 128] (pre-RoPE)."""
-    B = len(lens)
-    g = torch.Generator(device="cuda").manual_seed(seed)
-    kcs, vcs = [], []
-    for L in lens:
-        kc = torch.randn((L, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
-        vc = torch.randn((L, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+    """workloads.decode_batch_raw's step (caches drawn N(0,1) on the device), with each cache's
+    keys RoPE + QK-normalised at positions 0.. by the arm's own kernel."""
+    q, kn, vn, kcs, vcs = W.decode_batch_raw(lens, seed)
+    for kc in kcs:
         prep_normed(impl, kc, 0)
-        kcs.append(kc)
-        vcs.append(vc)
-    q = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
-    kn = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
-    vn = torch.randn((B, H, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
     return q, kn, vn, kcs, vcs
+
+
+def build_cfg1(impl, seed):
+    """workloads.cfg1_decode_case(seed) on the device: the new token at position 511 and the
+    caches' 511 earlier keys RoPE + QK-normalised by the arm's own kernel."""
+    q, kn, vn, kc, vc = (t.cuda() for t in W.cfg1_decode_case(seed))
+    prep_normed(impl, kc[:W.CFG1_LEN - 1], 0)
+    return q, kn, vn, [kc], [vc]
 
 
 def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
@@ -440,7 +443,11 @@ def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
                           device="cuda") if impl.kind == "nc" else None)
         set_steps = []
         for rs in range(R):
-            q, kn, vn, kcs, vcs = build_decode_batch(impl, lens, seed=2 + dist.rank + 1000 * rs)
+            # cfg1: set 0 is BASELINE's seed-0 draw; cfg3: the device draw seeded 2 (rank 0)
+            if name == "cfg1":
+                q, kn, vn, kcs, vcs = build_cfg1(impl, seed=1000 * rs)
+            else:
+                q, kn, vn, kcs, vcs = build_decode_batch(impl, lens, seed=2 + dist.rank + 1000 * rs)
             out = torch.empty((B, ROW), dtype=torch.bfloat16, device="cuda")
             if impl.kind == "nc":
                 kp = torch.tensor([t.data_ptr() for t in kcs], dtype=torch.int64, device="cuda")
@@ -630,9 +637,7 @@ def bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic):
         R = input_sets(n * (4 * C + 2 * rows) * ROW * 2)
         sets = []
         for rs in range(R):
-            g = torch.Generator(device="cuda").manual_seed(30 + dist.rank + 1000 * rs)
-            kslab = torch.randn((n, rows, H, D), generator=g, device="cuda").to(torch.bfloat16)
-            vslab = torch.randn((n, rows, H, D), generator=g, device="cuda").to(torch.bfloat16)
+            kslab, vslab = W.cfg4_cache_raw(n, rows, seed=30 + dist.rank + 1000 * rs)
             for i in range(n):
                 prep_normed(impl, kslab[i, :off], 0)
             sets.append((q0.clone(), k0.clone(), v0.clone(), kslab, vslab,
@@ -706,6 +711,9 @@ def main():
     ap.add_argument("--impl", choices=["nc", "reference"], default="nc")
     ap.add_argument("--no-extra", action="store_true", help="headline only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--clock-log-dir", default=None,
+                    help="directory for the raw nvidia-smi clock samples (default: the system "
+                         "temporary directory)")
     ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4", "gemm", "cfg5"],
                     default=None,
                     help="run one workload only (profiling); implies --no-cpu, no e2e")
@@ -739,7 +747,7 @@ def main():
             print(json.dumps({"only": args.only, "impl": args.impl, **r}), flush=True)
         dist.close()
         return
-    clocks = ClockSampler(dist.local)
+    clocks = ClockSampler(dist.local, args.clock_log_dir)
     clocks.start()
     head = bench_prefill(impl, dist, stepper, K, Wm, peaks, traffic)
     extra = {}

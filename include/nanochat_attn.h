@@ -72,7 +72,8 @@ int nc_rope_qknorm_append(void* q, const void* k, const void* v, void* k_cache, 
 /* out[s, h, :] = softmax(scale * Q[s,h] . K[j,h]^T) V[j,h] over keys j < kv_len with
  * j <= s + kv_offset; fp32 softmax, bf16 output.  seq_q > 1 runs the tcgen05 prefill
  * kernel; seq_q == 1 runs the split-KV decode kernel (its partial results live in a
- * per-device workspace the library allocates on first use and grows as needed).  A row with
+ * per-device workspace the library allocates on first use and grows as needed; see the
+ * drop-in notes below for what that implies).  A row with
  * no visible key gets NaN, as the reference's 0/0 does.
  * Replaces: kernels/flash_attention.cu:159-171 (flash_attention), declared src/model.h:26-27;
  * called from src/model.cpp:134-136. */
@@ -97,7 +98,8 @@ size_t nc_decode_workspace_bytes(int batch, int max_kv_len, int heads, int split
  *           with (2 + batch*heads) 32-bit counters (a work queue, an exit count and one split
  *           ticket per sequence and head) that each call leaves at zero, so a call can be
  *           captured in a CUDA graph and replayed.  Calls sharing one workspace must not
- *           overlap on the GPU.
+ *           overlap on the GPU.  A launch whose bounded wait gave up (nc_device_status
+ *           bit 0x100) can leave counters set: zero the workspace again before reusing it.
  * Replaces: the seq_len == 1 path of Model::attention (src/model.cpp:119-136): two
  * apply_rope_rmsnorm launches, two append copies and flash_attention, for one sequence. */
 int nc_decode_attention(void* out, const void* q, const void* k_new, const void* v_new,
@@ -142,8 +144,10 @@ int nc_decode_attention_overlap(void* out, const void* q, const void* k_new, con
  * device array inside the library (held by every GPU that loads it until exit), so:
  * batch <= 256 and max_kv_len <= 20480, else NC_ERR_TOO_LARGE; the split length grows as
  * needed to fit.  All calls on a device share the array and it keeps the last call's
- * contents: calls that overlap on the GPU race, so order them on one stream.  The first call
- * on a device sets the array up (and, with k_new, uploads the RoPE table); make it before any
+ * contents: calls that overlap on the GPU race, so order them on one stream.  Each call first
+ * clears the array's split counters with a memset on `stream`, so a call never inherits
+ * counters left set by an earlier launch whose bounded wait gave up.  The first call on a
+ * device sets the array up (and, with k_new, uploads the RoPE table); make it before any
  * stream capture.  Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
 int nc_decode_attention_noalloc(void* out, const void* q, const void* k_new, const void* v_new,
                                 void* const* k_caches, void* const* v_caches, const int* kv_len,

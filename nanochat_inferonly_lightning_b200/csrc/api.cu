@@ -28,10 +28,19 @@ std::mutex g_dev_mutex;
 struct DeviceState {
     const float2* rope_cs = nullptr;  // set once the table is on this device
     int* status = nullptr;            // device address of g_nc_status
-    void* ws = nullptr;               // decode workspace of the single-sequence entry point
-    size_t ws_bytes = 0;
 };
 DeviceState g_dev[kMaxDevices];
+
+// Decode workspaces of the single-sequence entry point (flash_attention with seq_q == 1), one
+// per (device, stream handle): calls on different streams never share split counters or
+// partial results.
+struct StreamWorkspace {
+    int dev;
+    cudaStream_t stream;
+    void* ws;
+    size_t bytes;
+};
+std::vector<StreamWorkspace> g_stream_ws;
 
 int cuda_fail(cudaError_t e) {
     t_last_cuda = (int)e;
@@ -221,8 +230,10 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
     return e == cudaSuccess ? NC_OK : cuda_fail(e);
 }
 
-// Library-owned workspace for the single-sequence entry point, one per device.
-int single_ws(int heads, int n_visible, void** ws, size_t* bytes) {
+// Library-owned workspace for the single-sequence entry point, one per (device, stream).
+// First use on a stream allocates it (cudaMalloc, so not under stream capture) and zeroes it
+// on that stream; growing it waits for that stream's earlier work, which may still use it.
+int single_ws(int heads, int n_visible, cudaStream_t stream, void** ws, size_t* bytes) {
     const int T = auto_split_len(1, std::max(n_visible, 1));
     const int splits = std::max(1, (n_visible + T - 1) / T);
     const size_t need = decode_workspace_bytes(1, splits, heads);
@@ -230,29 +241,35 @@ int single_ws(int heads, int n_visible, void** ws, size_t* bytes) {
     int st = current_device(&dev);
     if (st) return st;
     std::lock_guard<std::mutex> lk(g_dev_mutex);
-    DeviceState& d = g_dev[dev];
-    if (d.ws_bytes < need) {
-        if (d.ws) {
-            cudaError_t e = cudaDeviceSynchronize();  // an old launch may still use it
+    StreamWorkspace* w = nullptr;
+    for (StreamWorkspace& x : g_stream_ws)
+        if (x.dev == dev && x.stream == stream) w = &x;
+    if (!w) {
+        g_stream_ws.push_back(StreamWorkspace{dev, stream, nullptr, 0});
+        w = &g_stream_ws.back();
+    }
+    if (w->bytes < need) {
+        if (w->ws) {
+            cudaError_t e = cudaStreamSynchronize(stream);
             if (e != cudaSuccess) return cuda_fail(e);
-            cudaFree(d.ws);
-            d.ws = nullptr;
-            d.ws_bytes = 0;
+            cudaFree(w->ws);
+            w->ws = nullptr;
+            w->bytes = 0;
         }
         const size_t alloc = std::max(need, (size_t)1 << 20);
         void* p = nullptr;
         cudaError_t e = cudaMalloc(&p, alloc);
         if (e != cudaSuccess) return cuda_fail(e);
-        e = cudaMemset(p, 0, alloc);
+        e = cudaMemsetAsync(p, 0, alloc, stream);
         if (e != cudaSuccess) {
             cudaFree(p);
             return cuda_fail(e);
         }
-        d.ws = p;
-        d.ws_bytes = alloc;
+        w->ws = p;
+        w->bytes = alloc;
     }
-    *ws = d.ws;
-    *bytes = d.ws_bytes;
+    *ws = w->ws;
+    *bytes = w->bytes;
     return NC_OK;
 }
 
@@ -291,7 +308,7 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
         const int n_visible = std::min(kv_len, kv_offset + 1);
         void* ws = nullptr;
         size_t wsb = 0;
-        int st = single_ws(heads, std::max(n_visible, 0), &ws, &wsb);
+        int st = single_ws(heads, std::max(n_visible, 0), stream, &ws, &wsb);
         if (st) return st;
         return decode_common(out, Q, nullptr, nullptr, nullptr, nullptr, const_cast<void*>(K),
                              const_cast<void*>(V), nullptr, n_visible, 1, heads, scale,
@@ -306,6 +323,7 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
 int internal_rope_table(const float2** table) { return ensure_rope(table); }
 int internal_status_word(int** status) { return status_word(status); }
 int internal_cuda_fail(cudaError_t e) { return cuda_fail(e); }
+int internal_auto_split_len(int batch, int max_kv_len) { return auto_split_len(batch, max_kv_len); }
 
 }  // namespace nc
 

@@ -15,9 +15,13 @@
 //   * all calls on a device share the one array and it keeps the last call's contents, so
 //     calls whose kernels overlap on the GPU (different streams, or different host threads
 //     without ordering) race on it; order them on one stream;
-//   * the first call on a device does the set-up (it resolves the array's device address and
-//     clears the split counters, and the fused path uploads the RoPE table); make that first
-//     call before any stream capture.
+//   * the first call on a device does the set-up (it resolves the array's device address,
+//     and the fused path uploads the RoPE table); make that first call before any stream
+//     capture;
+//   * every call clears the split counters it will use (a memset on the caller's stream)
+//     before the decode kernel runs.  The kernel returns its counters to zero when it
+//     completes, but a launch whose bounded wait gave up leaves them set, and a caller of this
+//     entry point has no workspace of its own to re-zero.
 #include <algorithm>
 #include <mutex>
 
@@ -36,7 +40,7 @@ constexpr size_t kCounterBytes = 64u << 10;
 constexpr int kMaxDevices = 64;
 
 // Split counters at [0, 64 KiB), then the partial maxima/sums and the partial accumulators.
-// Zero at module load; the decode kernel leaves every counter at zero when it finishes.
+// Every call clears the counter words it uses before its kernel runs.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_setup_mutex;
@@ -47,15 +51,14 @@ unsigned char* g_scratch_addr[kMaxDevices] = {};
 int scratch_address(unsigned char** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return NC_ERR_CUDA;
+    if (e != cudaSuccess) return internal_cuda_fail(e);
     if (dev < 0 || dev >= kMaxDevices) return NC_ERR_INVALID_ARG;
     std::lock_guard<std::mutex> lk(g_setup_mutex);
     if (!g_scratch_addr[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) return NC_ERR_CUDA;
-        e = cudaMemset(p, 0, kCounterBytes);  // counters must start at zero
-        if (e != cudaSuccess) return NC_ERR_CUDA;
+        if (e != cudaSuccess) return internal_cuda_fail(e);
+        if (!p) return internal_cuda_fail(cudaErrorInvalidSymbol);
         g_scratch_addr[dev] = static_cast<unsigned char*>(p);
     }
     *out = g_scratch_addr[dev];
@@ -91,12 +94,13 @@ extern "C" int nc_decode_attention_noalloc(void* out, const void* q, const void*
         return NC_ERR_MISALIGNED;
     if (batch > kNoAllocMaxBatch || max_kv_len > kRopeMaxSeq) return NC_ERR_TOO_LARGE;
 
-    // Split length: about four CTAs per SM over the batch, doubled until the partial results
-    // fit in the array (a single split needs no partials at all).
+    // Split plan: the one nc_decode_attention makes for these sizes (same split length, same
+    // layout), with the split length doubled only while the partial results would not fit in
+    // the array (a single split needs no partials at all).  The per-head layout's calls
+    // (<= 8 sequences, <= 8192 keys in all) always fit: at most 128 splits x 31 heads.
     const int L = std::max(max_kv_len, 1);
-    const long long est = batch > 1 ? (long long)batch * L / 2 : L;
-    long long T = std::max<long long>(16, ((est + 591) / 592 + 15) / 16 * 16);
-    T = std::min<long long>(T, 1024);
+    const int T_auto = internal_auto_split_len(batch, L);
+    long long T = T_auto;
     const size_t room = kNoAllocScratchBytes - kCounterBytes;
     int splits = (int)((L + T - 1) / T);
     while (splits > 1 && partial_bytes(batch, splits, heads) > room) {
@@ -104,6 +108,8 @@ extern "C" int nc_decode_attention_noalloc(void* out, const void* q, const void*
         splits = (int)((L + T - 1) / T);
     }
     if (splits > 1 && partial_bytes(batch, splits, heads) > room) return NC_ERR_TOO_LARGE;
+    const size_t counter_bytes = decode_counter_words(batch, heads) * sizeof(unsigned);
+    if (counter_bytes > kCounterBytes) return NC_ERR_TOO_LARGE;
 
     unsigned char* base = nullptr;
     int st = scratch_address(&base);
@@ -129,10 +135,14 @@ extern "C" int nc_decode_attention_noalloc(void* out, const void* q, const void*
     a.scale_log2 = scale * kLog2e;
     a.split_len = (int)T;
     a.max_splits = splits;
+    a.head_layout = decode_use_head_layout(batch, max_kv_len, T == T_auto ? 0 : (int)T) ? 1 : 0;
     a.counters = reinterpret_cast<unsigned*>(base);
     a.part_ml = reinterpret_cast<float2*>(base + kCounterBytes);
     a.part_o = reinterpret_cast<float*>(
         base + kCounterBytes + round256((size_t)batch * splits * heads * sizeof(float2)));
-    cudaError_t e = launch_decode(a, stream);
-    return e == cudaSuccess ? NC_OK : NC_ERR_CUDA;
+    // Counters start at zero for this call whatever an earlier call left behind.
+    cudaError_t e = cudaMemsetAsync(base, 0, counter_bytes, stream);
+    if (e != cudaSuccess) return internal_cuda_fail(e);
+    e = launch_decode(a, stream);
+    return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }

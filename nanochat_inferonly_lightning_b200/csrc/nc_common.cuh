@@ -279,5 +279,8 @@ int internal_rope_table(const float2** table);
 int internal_status_word(int** status);
 // Records `e` as this thread's last CUDA error and returns NC_ERR_CUDA.
 int internal_cuda_fail(cudaError_t e);
+// Keys per split that nc_decode_attention picks for `batch` sequences of up to `max_kv_len`
+// keys when the caller passes split_len 0.
+int internal_auto_split_len(int batch, int max_kv_len);
 
 }  // namespace nc

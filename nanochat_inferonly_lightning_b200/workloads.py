@@ -38,13 +38,28 @@ CFG1_POS = 511
 CFG1_LEN = 512
 
 
-def cfg1_inputs():
+def cfg1_inputs(seed=0):
     """Q [1,17,128] (pre-RoPE), K/V [512,17,128] (K pre-RoPE), seed 0."""
-    g = torch.Generator().manual_seed(0)
+    g = torch.Generator().manual_seed(seed)
     q = randn_bf16((1, HEADS, HEAD_DIM), g)
     k = randn_bf16((CFG1_LEN, HEADS, HEAD_DIM), g)
     v = randn_bf16((CFG1_LEN, HEADS, HEAD_DIM), g)
     return q, k, v
+
+
+def cfg1_decode_case(seed=0):
+    """cfg1 as the decode step the benchmark times, from cfg1_inputs(seed): the new token at
+    position 511 (q, k_new, v_new [1,17,128], pre-RoPE) and the caches [512,17,128] holding the
+    keys and values of positions 0..510 (row 511 zero: the step appends the new token there).
+    The cache keys are pre-RoPE here: callers apply RoPE + QK-norm to rows 0..510 at positions
+    0..510 with their own kernel, as a model's earlier steps would have.  CPU tensors."""
+    q, k, v = cfg1_inputs(seed)
+    n = CFG1_LEN - 1
+    kc = torch.zeros((CFG1_LEN, HEADS, HEAD_DIM), dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kc[:n] = k[:n]
+    vc[:n] = v[:n]
+    return q, k[n:], v[n:], kc, vc
 
 
 CFG1_BYTES = decode_bytes([CFG1_LEN])  # 4,460,800
@@ -80,6 +95,28 @@ def cfg3_bytes(kv_lens=None):
     return decode_bytes(kv_lens if kv_lens is not None else cfg3_kv_lens())
 
 
+def decode_batch_raw(lens, seed, device="cuda"):
+    """A decode step over independent sequences (cfg3 and the like), drawn N(0,1) from a torch
+    generator on `device` seeded with `seed`, in this order: per sequence its K cache then its
+    V cache ([L_i,17,128]), then the new tokens' q, k_new, v_new ([B,17,128], pre-RoPE).  The
+    cache keys are pre-RoPE: callers apply RoPE + QK-norm at positions 0.. with their own kernel
+    (rows up to L_i - 2 are read; row L_i - 1 receives the appended new key)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def rnd(shape):
+        return torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+    kcs, vcs = [], []
+    for L in lens:
+        kcs.append(rnd((L, HEADS, HEAD_DIM)))
+        vcs.append(rnd((L, HEADS, HEAD_DIM)))
+    B = len(lens)
+    q = rnd((B, HEADS, HEAD_DIM))
+    kn = rnd((B, HEADS, HEAD_DIM))
+    vn = rnd((B, HEADS, HEAD_DIM))
+    return q, kn, vn, kcs, vcs
+
+
 # ---------------------------------------------------------------------------------- cfg4
 CFG4_BATCH = 4
 CFG4_OFFSET = 1536
@@ -94,6 +131,17 @@ def cfg4_chunk_inputs(batch=CFG4_BATCH, chunk=CFG4_CHUNK, seed=3):
     k = randn_bf16((batch, chunk, HEADS, HEAD_DIM), g)
     v = randn_bf16((batch, chunk, HEADS, HEAD_DIM), g)
     return q, k, v
+
+
+def cfg4_cache_raw(n, rows=CFG4_OFFSET + CFG4_CHUNK, seed=30, device="cuda"):
+    """K and V cache slabs [n, rows, 17, 128] for the chunked prefill, N(0,1) from a torch
+    generator on `device` (K slab drawn first).  Rows [0, 1536) stand for the cached prefix:
+    callers apply RoPE + QK-norm to their keys at positions 0..1535 with their own kernel; the
+    chunk's append writes rows [1536, 2048)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    kslab = torch.randn((n, rows, HEADS, HEAD_DIM), generator=g, device=device).to(torch.bfloat16)
+    vslab = torch.randn((n, rows, HEADS, HEAD_DIM), generator=g, device=device).to(torch.bfloat16)
+    return kslab, vslab
 
 
 def shard(n_items, rank, world):

@@ -12,11 +12,31 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT = os.path.join(OUT_DIR, "libref_attn.so")
-DEFAULT_REF = "/root/reference"
+
+
+def reference_root():
+    """The reference project's source tree: $NC_REFERENCE_ROOT, else the `reference_path` that
+    BASELINE.json at the repository root records, else None."""
+    env = os.environ.get("NC_REFERENCE_ROOT")
+    if env:
+        return env
+    import json
+
+    bj = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+    try:
+        with open(bj) as f:
+            return json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
 
 
 def build(ref_root=None, force=False, verbose=True):
-    ref_root = ref_root or os.environ.get("NC_REFERENCE_ROOT", DEFAULT_REF)
+    ref_root = ref_root or reference_root()
+    if not ref_root:
+        if verbose:
+            print("[oracle] no reference tree given (set NC_REFERENCE_ROOT); keeping existing "
+                  f"{OUT}")
+        return os.path.exists(OUT)
     kdir = os.path.join(ref_root, "kernels")
     sdir = os.path.join(ref_root, "src")
     srcs = [os.path.join(kdir, "rope.cu"), os.path.join(kdir, "flash_attention.cu"),

@@ -29,6 +29,10 @@ fp32 floor and reports the free-running identity.
 
 Weights are random N(0, 0.02) in bf16 (seed 4), prompts are 256 token ids uniform in
 [0, 65536) (cfg5); 8 prompts, 32 greedy steps each.
+
+A second test runs the batched engine that bench.py's cfg5 measures (engine.BatchedEngine:
+this library's GEMMs with fused norms, decode attention, embedding and argmax in a captured
+CUDA graph) against the same reference arm, under the same near-tie rule.
 """
 import ctypes
 import math
@@ -185,7 +189,14 @@ def setup():
     assert nc.device_status(reset=True) == 0, "a kernel's bounded wait gave up"
 
 
-def test_greedy_decode_against_reference(setup):
+@pytest.fixture(scope="module")
+def reference_runs(setup):
+    """The reference arm's 32 greedy tokens and its logits at every step, per prompt."""
+    ref, nc, w, prompts = setup
+    return [Engine(w, ref, "reference").generate(prompt, STEPS) for prompt in prompts]
+
+
+def test_greedy_decode_against_reference(setup, reference_runs):
     """Per prompt, the reference arm decodes 32 greedy tokens; the library and fp32 arms are
     fed the same tokens (teacher forcing).  Asserted: (1) the library picks the reference's
     token at every step except where the reference's logits of the two tokens are within
@@ -195,7 +206,7 @@ def test_greedy_decode_against_reference(setup):
     ref, nc, w, prompts = setup
     report, dev_lib, dev_f32, max_lib = [], [], [], 0.0
     for n, prompt in enumerate(prompts):
-        want, lref = Engine(w, ref, "reference").generate(prompt, STEPS)
+        want, lref = reference_runs[n]
         row = dict(prompt=n, steps=len(want))
         for arm in ("library", "fp32"):
             eng = lambda: Engine(w, ref, arm, nc)
@@ -222,3 +233,50 @@ def test_greedy_decode_against_reference(setup):
     mean_lib, mean_f32 = sum(dev_lib) / len(dev_lib), sum(dev_f32) / len(dev_f32)
     assert mean_lib <= 1.25 * mean_f32 + 1e-3, (mean_lib, mean_f32)
     assert max_lib < 0.25, max_lib
+
+
+def test_engine_greedy_against_reference(setup, reference_runs):
+    """The batched engine as bench.py's cfg5 runs it (engine.BatchedEngine: all 8 prompts in
+    one batched prompt pass, then a CUDA-graph-captured decode step with the skinny tcgen05
+    GEMMs and their fused RMSNorm / residual / ReLU^2 / tanh cap, the fused decode attention,
+    the embedding + RMSNorm kernel and the device argmax) against the reference arm above, on
+    the same seed-4 weights and prompts.  Teacher forcing: after each step every sequence's
+    next input is the reference's token.  Asserted at every step of every sequence: the
+    engine's token is the reference's, or the reference's logits of the two tokens are within
+    8 bf16 ulps.  Reported: per-step agreement and the margin of every disagreement."""
+    from nanochat_inferonly_lightning_b200 import engine as E
+
+    ref, nc, w, prompts = setup
+    B = len(prompts)
+    wants = [r[0] for r in reference_runs]
+    lrefs = [r[1] for r in reference_runs]
+    n_steps = min(len(x) for x in wants)
+    eng = E.BatchedEngine(w, B, PROMPT_LEN + STEPS + 8)
+    first = eng.prefill(torch.tensor(prompts, dtype=torch.int64, device="cuda"))
+    picks = [first.to(torch.int64).cpu().tolist()]
+    logits = [None]  # step 0's logits come from the prompt pass (checked through its margin)
+    for t in range(1, n_steps):
+        eng.tok.copy_(torch.tensor([wants[b][t - 1] for b in range(B)], dtype=torch.int32))
+        if t == 1:
+            eng.capture()  # eager step (its result is this step's), then the graph capture
+        else:
+            eng.step()
+        picks.append(eng.tok.to(torch.int64).cpu().tolist())
+        logits.append(eng.logits.float().cpu())
+    torch.cuda.synchronize()
+    agree, flips = [], []
+    for t in range(n_steps):
+        same = 0
+        for b in range(B):
+            a, want = picks[t][b], wants[b][t]
+            if a == want:
+                same += 1
+                continue
+            lr = lrefs[b][t]
+            gap = (float(lr[want]) - float(lr[a])) / bf16_ulp(float(lr[want]))
+            flips.append(dict(step=t, seq=b, engine=a, reference=want, gap_ulps=round(gap, 1)))
+            assert gap <= 8.0, (f"seq {b} step {t}: engine picks {a}, reference {want}; reference "
+                                f"logits {gap:.1f} bf16 ulps apart")
+        agree.append(same)
+    print("engine vs reference: agreeing sequences per step", agree, "flips", flips)
+    assert sum(agree) >= 0.9 * B * n_steps, agree
