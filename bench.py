@@ -559,6 +559,87 @@ def bench_cfg5(dist):
                     "4.15 GB of weights read per step"}
 
 
+def write_reference_weights(path, seed=4):
+    """Seed-4 random weights (engine.Weights, N(0, 0.02) bf16) written in the reference's
+    weights.bin layout (src/model.cpp:17-35): embedding, per layer q, k, v, o, MLP up, MLP
+    down, then the LM head, raw bf16."""
+    from nanochat_inferonly_lightning_b200 import engine as E
+
+    w = E.Weights(seed=seed)
+    with open(path, "wb") as f:
+        def put(t):
+            t.contiguous().view(torch.int16).cpu().numpy().tofile(f)
+
+        put(w.embed)
+        for l in w.layers:
+            for key in ("q", "k", "v", "o", "up", "down"):
+                put(l[key])
+        put(w.lm_head)
+    del w
+    torch.cuda.empty_cache()
+
+
+def bench_cfg5_reference(dist):
+    """cfg5 on the reference's own engine (src/model.cpp + src/engine.cpp with its CUTLASS GEMM
+    and its attention kernels, rebuilt for sm_100a into oracle/_ref/libref_model_ref.so): the
+    same seed-4 weights, loaded from a weights.bin file by the reference's loader, and the same
+    8 prompts, decoded one sequence after another with Engine::generate at temperature 0
+    (batch 1, as the reference serves).  Engine::generate synchronises with the host after
+    every token, so the figure is wall-clock time around each call: decode tok/s = generated
+    tokens after the first / (time of a 256-token generation - time of its prompt pass alone)."""
+    import tempfile
+
+    so = os.path.join(ROOT, "oracle", "_ref", "libref_model_ref.so")
+    if not os.path.exists(so):
+        return {"unavailable": "oracle/_ref/libref_model_ref.so not built"}
+    lib = ctypes.CDLL(so)
+    vp, ip = ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)
+    lib.refe_create.restype = vp
+    lib.refe_load.argtypes = [vp, ctypes.c_char_p]
+    lib.refe_generate_greedy.argtypes = [vp, ip, ctypes.c_int, ctypes.c_int, ip]
+    lib.refe_destroy.argtypes = [vp]
+    batch, prompt_len, steps = 8, 256, 256
+    tmpdir = tempfile.mkdtemp(prefix="nc_ref_weights_")
+    path = os.path.join(tmpdir, "weights.bin")
+    try:
+        write_reference_weights(path)
+        e = lib.refe_create()
+        if not e or lib.refe_load(e, path.encode()) != 0:
+            return {"unavailable": "reference engine failed to load the weights file"}
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+        os.rmdir(tmpdir)
+    g = torch.Generator().manual_seed(4 + dist.rank)
+    prompts = torch.randint(0, 65536, (batch, prompt_len), generator=g).tolist()
+    out = (ctypes.c_int * steps)()
+    arr0 = (ctypes.c_int * prompt_len)(*prompts[0])
+    lib.refe_generate_greedy(e, arr0, prompt_len, 4, out)  # warm-up (module and cache set-up)
+    t_full, t_prompt, n_gen = 0.0, 0.0, 0
+    for pr in prompts:
+        arr = (ctypes.c_int * prompt_len)(*pr)
+        t0 = time.perf_counter()
+        lib.refe_generate_greedy(e, arr, prompt_len, 1, out)  # prompt pass + first token
+        t1 = time.perf_counter()
+        n = lib.refe_generate_greedy(e, arr, prompt_len, steps, out)
+        t2 = time.perf_counter()
+        t_prompt += t1 - t0
+        t_full += t2 - t1
+        n_gen += max(n - 1, 0)
+    lib.refe_destroy(e)
+    torch.cuda.synchronize()
+    dec = max(t_full - t_prompt, 1e-9)
+    return {"value": n_gen / dec, "unit": "tok/s (decode)",
+            "ms_per_decode_step": dec / max(n_gen, 1) * 1e3,
+            "prompt_pass_ms": t_prompt / batch * 1e3, "sequences": batch,
+            "prompt_len": prompt_len, "decode_steps": steps,
+            "timing": "wall clock around Engine::generate (host-synchronous per token), 8 "
+                      "sequences one after another, batch 1; decode time = full generation "
+                      "minus its prompt pass",
+            "engine": "reference src/model.cpp + src/engine.cpp, CUTLASS GEMM (4.5 headers), "
+                      "reference attention kernels, sm_100a"}
+
+
 GEMM_SHAPES = (  # decode-step GEMMs of the full architecture (src/model.cpp:110-177)
     ("qkv", 3 * 2176, 2176, "NORM_INPUT", 2176),
     ("o", 2176, 2176, "RESIDUAL", 0),
@@ -741,7 +822,8 @@ def main():
                                            W.cfg3_kv_lens(), "cfg3"),
               "cfg4": lambda: bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic),
               "gemm": lambda: bench_gemm(dist, stepper, K, Wm, peaks, traffic),
-              "cfg5": lambda: bench_cfg5(dist)}[args.only]
+              "cfg5": (lambda: bench_cfg5(dist)) if impl.kind == "nc"
+                      else (lambda: bench_cfg5_reference(dist))}[args.only]
         r = fn()
         if dist.rank == 0:
             print(json.dumps({"only": args.only, "impl": args.impl, **r}), flush=True)
@@ -761,6 +843,8 @@ def main():
         if impl.kind == "nc":
             extra["decode_step_gemms"] = bench_gemm(dist, stepper, K, Wm, peaks, traffic)
             extra["cfg5_e2e_generation"] = bench_cfg5(dist)
+        else:
+            extra["cfg5_e2e_generation"] = bench_cfg5_reference(dist)
     clk = clocks.stop()
 
     line = {

@@ -25,6 +25,7 @@ def _built_libraries():
     pkg_build.build(verbose=False)
     orc_build.build(verbose=False)
     build_ref.build(verbose=False)
+    build_ref.build_model(verbose=False)
     yield
 
 
