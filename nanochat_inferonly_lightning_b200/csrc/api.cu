@@ -185,7 +185,11 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
     const int max_splits = std::max(1, (max_kv_len + T - 1) / T);
     if (max_splits > 65535) return NC_ERR_INVALID_ARG;
     const size_t need = decode_workspace_bytes(batch, max_splits, heads);
-    if (max_splits > 1 && (!ws || ws_bytes < need)) return NC_ERR_WORKSPACE;
+    const bool head_layout = decode_use_head_layout(batch, max_kv_len, split_len);
+    // Splits combined through a global workspace: all but the per-head layout's cluster case.
+    const bool uses_ws =
+        max_splits > 1 && !(head_layout && decode_head_cluster(max_splits, overlap != 0));
+    if (uses_ws && (!ws || ws_bytes < need)) return NC_ERR_WORKSPACE;
     DecodeArgs a{};
     if (k_new) {
         int st = ensure_rope(&a.rope_cs);
@@ -213,12 +217,12 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
         a.pages_per_seq = pg->pages_per_seq;
         a.num_pages = pg->num_pages;
     }
-    a.head_layout = decode_use_head_layout(batch, max_kv_len, split_len) ? 1 : 0;
+    a.head_layout = head_layout ? 1 : 0;
     a.overlap = overlap && a.head_layout ? 1 : 0;
     a.scale_log2 = scale * kLog2e;
     a.split_len = T;
     a.max_splits = max_splits;
-    if (ws) {
+    if (ws && uses_ws) {
         WsLayout w = carve_ws(ws, batch, max_splits, heads);
         a.part_o = w.part_o;
         a.part_ml = w.part_ml;
@@ -308,8 +312,15 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
         const int n_visible = std::min(kv_len, kv_offset + 1);
         void* ws = nullptr;
         size_t wsb = 0;
-        int st = single_ws(heads, std::max(n_visible, 0), stream, &ws, &wsb);
-        if (st) return st;
+        // Up to 16 splits of the per-head layout combine in a thread-block cluster and need no
+        // workspace; longer calls use this stream's library-owned workspace.
+        const int T = auto_split_len(1, std::max(n_visible, 1));
+        const int splits = std::max(1, (std::max(n_visible, 0) + T - 1) / T);
+        if (splits > 1 && !(decode_use_head_layout(1, std::max(n_visible, 0), 0) &&
+                            decode_head_cluster(splits, false))) {
+            int st = single_ws(heads, std::max(n_visible, 0), stream, &ws, &wsb);
+            if (st) return st;
+        }
         return decode_common(out, Q, nullptr, nullptr, nullptr, nullptr, const_cast<void*>(K),
                              const_cast<void*>(V), nullptr, n_visible, 1, heads, scale,
                              std::max(n_visible, 0), 0, ws, wsb, stream);

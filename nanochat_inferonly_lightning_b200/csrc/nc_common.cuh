@@ -241,6 +241,13 @@ inline bool decode_use_head_layout(int batch, int max_kv_len, int split_len) {
     if (split_len) return split_len <= kDecodeHeadSplit;
     return (long long)batch * max_kv_len <= kDecodeHeadMaxKeys;
 }
+// Per-head calls with 2..16 splits combine them inside a thread-block cluster (distributed
+// shared memory), without global partials, tickets or workspace; not when the call overlaps
+// the kernel before it (programmatic dependent launch).
+constexpr int kDecodeHeadMaxCluster = 16;
+inline bool decode_head_cluster(int max_splits, bool overlap) {
+    return !overlap && max_splits >= 2 && max_splits <= kDecodeHeadMaxCluster;
+}
 size_t decode_workspace_bytes(int batch, int max_splits, int heads);
 // 32-bit words at the start of the decode workspace: two work-queue words, then one split
 // ticket per (sequence, head).  All zero between launches.
