@@ -261,6 +261,18 @@ enum {
 int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual, int M, int N,
                    int K, int flags, float cap, int seg_cols, int splits, cudaStream_t stream);
 
+/* The same product and fused steps for any M, laid out for the prompt pass (M = prompt tokens,
+ * hundreds to thousands of rows): out[M, N] = epilogue(x[M, K] . w[N, K]^T) on a persistent
+ * tcgen05 kernel with 128 x 256 output tiles, both operands staged by TMA, fp32 accumulation
+ * in tensor memory, one bf16 rounding.  Same flags, order and seg_cols as nc_gemm_skinny.
+ * Requirements: N % 8 == 0, K % 8 == 0, seg_cols % 8 == 0; x, w, out and residual 16-byte
+ * aligned; out must not overlap x (residual may equal out).  Deterministic.
+ * Replaces: gemm_half / gemm_half_residual for M > 16 (kernels/gemm.cu:14-51, the 128 x 128
+ * CUTLASS tiles) at the prompt call sites src/model.cpp:114-116, :139, :149-150, :153, together
+ * with the rmsnorm / relu_squared launches around them. */
+int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M, int N, int K,
+            int flags, float cap, int seg_cols, cudaStream_t stream);
+
 /* ----------------------------------------------------------------------------------------
  * The two ends of a decode step.
  * out[r, :] = RMSNorm(table[tokens[r], :]) (eps 1e-6, one bf16 rounding): the embedding gather

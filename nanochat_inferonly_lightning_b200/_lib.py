@@ -71,6 +71,8 @@ SIGNATURES = {
                                c_void_p, c_void_p]),
     "nc_gemm_skinny": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_int, c_float, c_int, c_int, c_void_p]),
+    "nc_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                        c_float, c_int, c_void_p]),
 }
 
 # C++ entry points with the reference's names (namespace nanochat, C++ linkage).

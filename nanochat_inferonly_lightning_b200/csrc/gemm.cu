@@ -308,6 +308,293 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 }
 
 // ---------------------------------------------------------------------------------------
+// Prompt-pass GEMM (any M, sized for M in the hundreds to thousands): persistent, one CTA per
+// SM, 128 x 256 output tiles (one tcgen05.mma of M = 128 rows of x, N = 256 output features,
+// K = 16 per step), x and w boxes staged by TMA (no multicast) through a 4-stage ring of
+// 48 KB stages, and two 256-column accumulators in TMEM so that the epilogue of one tile
+// overlaps the MMAs of the next.  Tiles are numbered with the row block fastest, so the CTAs
+// working at the same time share each weight tile through L2.
+// Warp roles (192 threads): warp 0 lane 0 issues TMA, warp 1 the MMAs (elected lane) and owns
+// TMEM, warps 2-5 the epilogue (warp w reads TMEM lanes 32*(w%4)..+31 = the tile's rows):
+// while a tile's MMAs run they compute each row's RMSNorm scale from x (NC_GEMM_NORM_INPUT),
+// then read the accumulator 32 columns at a time, hand it back once all 256 are read, apply
+// the fused steps of finish() on the fp32 values and store 16-byte groups of 8 outputs.
+// ---------------------------------------------------------------------------------------
+constexpr int kTThreads = 192;
+constexpr int kTBM = 128;
+constexpr int kTBN = 256;
+constexpr int kTStages = 4;
+constexpr int kTABytes = kTBM * kTileK * 2;  // 16 KB
+constexpr int kTBBytes = kTBN * kTileK * 2;  // 32 KB
+constexpr uint32_t kTTmemCols = 512;
+
+struct TileTail {
+    uint64_t full[kTStages];
+    uint64_t empty[kTStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t drain;
+    float rs[kTBM];  // RMSNorm scale of each row of the current tile (its epilogue warp's rows)
+    uint32_t tmem;
+    int abort;
+};
+constexpr int kTSmemBytes = kTStages * (kTABytes + kTBBytes) + (int)sizeof(TileTail) + 1024;
+static_assert(kTSmemBytes <= 227 * 1024, "shared memory budget");
+
+struct TileParams {
+    bf16* out;
+    const bf16* x;
+    const bf16* residual;
+    int M, N, K;
+    int kb_total;
+    int m_tiles, n_tiles, tiles;
+    int n_per;  // > 0: CTA c keeps row block c % m_tiles and takes its column tiles
+                // c / m_tiles, + n_per, ...; 0: tiles t = c, c + grid, ... (row block fastest)
+    int flags;
+    float cap;
+    int seg_cols;
+    int* status;
+};
+
+// The tiles of one CTA, in order (every role walks the same sequence).
+struct TileWalk {
+    int mt, nt, t;
+    __device__ __forceinline__ void start(const TileParams& p) {
+        if (p.n_per) {
+            mt = blockIdx.x % p.m_tiles;
+            nt = blockIdx.x / p.m_tiles;
+        } else {
+            t = blockIdx.x;
+            mt = t % p.m_tiles;
+            nt = t / p.m_tiles;
+        }
+    }
+    __device__ __forceinline__ bool valid(const TileParams& p) const {
+        return p.n_per ? nt < p.n_tiles : t < p.tiles;
+    }
+    __device__ __forceinline__ void next(const TileParams& p) {
+        if (p.n_per) {
+            nt += p.n_per;
+        } else {
+            t += gridDim.x;
+            mt = t % p.m_tiles;
+            nt = t / p.m_tiles;
+        }
+    }
+};
+
+constexpr int kTagTEmpty = 0x51, kTagTFull = 0x52, kTagTAccFull = 0x53, kTagTAccEmpty = 0x54,
+              kTagTDrainLoad = 0x55, kTagTDrainMma = 0x56;
+
+__global__ void __launch_bounds__(kTThreads, 1)
+    gemm_tile_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const TileParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = base;                          // stage i at sA + i * kTABytes
+    uint8_t* sB = base + kTStages * kTABytes;    // stage i at sB + i * kTBBytes
+    TileTail* tail = reinterpret_cast<TileTail*>(sB + kTStages * kTBBytes);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kTStages; ++i) {
+            mbar_init(&tail->full[i], 1);
+            mbar_init(&tail->empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tail->acc_full[i], 1);
+            mbar_init(&tail->acc_empty[i], 128);
+        }
+        mbar_init(&tail->drain, 1);
+        tail->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmX);
+        prefetch_tmap(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tail->tmem, kTTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem;
+    volatile int* abort_flag = &tail->abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int it = 0;  // running k-block count of this CTA: stage it % kTStages
+            bool ok = true;
+            TileWalk tw;
+            for (tw.start(p); ok && tw.valid(p); tw.next(p)) {
+                const int m0 = tw.mt * kTBM;
+                const int n0 = tw.nt * kTBN;
+                for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+                    const int st = it % kTStages;
+                    if (it >= kTStages &&
+                        !(ok = mbar_wait(&tail->empty[st], ((it / kTStages) - 1) & 1, abort_flag,
+                                         p.status, kTagTEmpty)))
+                        break;
+                    mbar_arrive_expect_tx(&tail->full[st], kTABytes + kTBBytes);
+                    tma_load_2d(sA + st * kTABytes, &tmX, &tail->full[st], kb * kTileK, m0);
+                    tma_load_2d(sB + st * kTBBytes, &tmW, &tail->full[st], kb * kTileK, n0);
+                }
+            }
+            if (!ok) {
+                // Leaving early: wait for the copies still in flight into this CTA's ring.
+                for (int i = max(it - kTStages, 0); i < it; ++i)
+                    mbar_wait_drain(&tail->full[i % kTStages], (i / kTStages) & 1, p.status,
+                                    kTagTDrainLoad);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        const uint32_t idesc = idesc_bf16_f32(kTBM, kTBN, false);  // both operands K-major
+        const uint64_t dA0 = smem_desc_sw128(smem_u32(sA), 16, 1024);
+        const uint64_t dB0 = smem_desc_sw128(smem_u32(sB), 16, 1024);
+        bool ok = true;
+        int it = 0, lt = 0;
+        TileWalk tw;
+        for (tw.start(p); ok && tw.valid(p); tw.next(p), ++lt) {
+            const int buf = lt & 1;
+            // The accumulator buffer is free once the epilogue read the tile before last.
+            if (lt >= 2 && !(ok = __all_sync(0xFFFFFFFFu,
+                                             mbar_wait(&tail->acc_empty[buf], ((lt >> 1) - 1) & 1,
+                                                       abort_flag, p.status, kTagTAccEmpty))))
+                break;
+            tc_fence_after();
+            const uint32_t acc = tmem + buf * kTBN;
+            for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+                const int st = it % kTStages;
+                if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tail->full[st], (it / kTStages) & 1,
+                                                             abort_flag, p.status, kTagTFull))))
+                    break;
+                tc_fence_after();
+                const uint64_t dA = dA0 + (uint64_t)(st * (kTABytes >> 4));
+                const uint64_t dB = dB0 + (uint64_t)(st * (kTBBytes >> 4));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)  // 16 K-elements = 32 bytes per MMA
+                    mma_ss_warp(acc, dA + kk * 2, dB + kk * 2, idesc, (kb | kk) ? 1u : 0u);
+                mma_commit_warp(&tail->empty[st]);
+            }
+            if (ok) mma_commit_warp(&tail->acc_full[buf]);
+        }
+        // Leave only once every MMA issued above has completed: TMEM is released below.
+        mma_commit_warp(&tail->drain);
+        mbar_wait_drain(&tail->drain, 0, p.status, kTagTDrainMma);
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // the tile row (TMEM lane) this thread owns
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        int lt = 0;
+        float rs = 1.f;
+        TileWalk tw;
+        for (tw.start(p); tw.valid(p); tw.next(p), ++lt) {
+            const int buf = lt & 1;
+            const int m = tw.mt * kTBM + r;
+            const int n0 = tw.nt * kTBN;
+            // RMSNorm scale of the warp's 32 rows (reference kernels/rmsnorm.cu:17-48: fp32
+            // sum of squares, rsqrt(sum / K + 1e-6)), while the tile's MMAs run: four rows at a
+            // time, the 32 lanes reading consecutive 16-byte pieces of each (coalesced), then a
+            // butterfly sum.  A CTA that keeps one row block computes them once.
+            if ((p.flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
+                const int mq = tw.mt * kTBM + quarter * 32;
+                for (int r4 = 0; r4 < 32; r4 += 4) {
+                    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int mr = mq + r4 + u;
+                        if (mr >= p.M) continue;
+                        const uint4* row = reinterpret_cast<const uint4*>(p.x + (size_t)mr * p.K);
+                        for (int c = lane; c < p.K / 8; c += 32) {
+                            float f[8];
+                            bf16x8_to_f32(__ldg(row + c), f);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
+                    }
+                    if (lane < 4) {
+                        const float v = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
+                        tail->rs[quarter * 32 + r4 + lane] = rsqrtf(v / (float)p.K + kNormEps);
+                    }
+                }
+                __syncwarp();
+                rs = tail->rs[quarter * 32 + lane];
+                __syncwarp();  // read before the next tile's scales overwrite it
+            }
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&tail->acc_full[buf], (lt >> 1) & 1, abort_flag,
+                                                   p.status, kTagTAccFull)))
+                break;
+            tc_fence_after();
+            for (int c = 0; c < kTBN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32_sync(tmem + buf * kTBN + 32 * c + lane_base, v);
+                if (c == kTBN / 32 - 1) {
+                    // Every column of this accumulator has been read: the tile after next may
+                    // accumulate into it.
+                    tc_fence_before();
+                    mbar_arrive(&tail->acc_empty[buf]);
+                }
+                if (m >= p.M) continue;
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) {
+                    const int n = n0 + 32 * c + 8 * g8;
+                    if (n >= p.N) break;
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[8 * g8 + e]);
+                    if (p.flags & NC_GEMM_NORM_INPUT) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] *= rs;
+                    }
+                    if (p.flags & NC_GEMM_RESIDUAL) {
+                        float rr[8];
+                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n), rr);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] += rr[e];
+                    }
+                    if (p.flags & NC_GEMM_RELU2) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float y = fmaxf(f[e], 0.f);
+                            f[e] = y * y;
+                        }
+                    }
+                    if (p.flags & NC_GEMM_TANH_CAP) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = p.cap * tanhf(f[e] / p.cap);
+                    }
+                    const int seg = p.seg_cols;
+                    bf16* dst = p.out + (size_t)(n / seg) * ((size_t)p.M * seg) + (size_t)m * seg +
+                                (n % seg);
+                    *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(f);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -488,6 +775,68 @@ int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual
     if (mp == 16) e = launch_mp<16>(mw, mx, p, g, dev, stream);
     else if (mp == 32) e = launch_mp<32>(mw, mx, p, g, dev, stream);
     else e = launch_mp<64>(mw, mx, p, g, dev, stream);
+    return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
+}
+
+int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M, int N, int K,
+            int flags, float cap, int seg_cols, cudaStream_t stream) {
+    using namespace nc;
+    if (M < 1 || N < 8 || (N & 7) || K < 8 || (K & 7)) return NC_ERR_INVALID_ARG;
+    if (flags & ~(NC_GEMM_NORM_INPUT | NC_GEMM_RESIDUAL | NC_GEMM_RELU2 | NC_GEMM_TANH_CAP))
+        return NC_ERR_INVALID_ARG;
+    if (!out || !x || !w || ((flags & NC_GEMM_RESIDUAL) && !residual)) return NC_ERR_INVALID_ARG;
+    if ((flags & NC_GEMM_TANH_CAP) && !(cap > 0.f)) return NC_ERR_INVALID_ARG;
+    if (seg_cols == 0) seg_cols = N;
+    if (seg_cols < 8 || (seg_cols & 7) || N % seg_cols) return NC_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(residual) & 15))
+        return NC_ERR_MISALIGNED;
+    if (overlaps(out, (size_t)M * N * 2, x, (size_t)M * K * 2)) return NC_ERR_INVALID_ARG;
+    if ((flags & NC_GEMM_RESIDUAL) && residual != out &&
+        overlaps(out, (size_t)M * N * 2, residual, (size_t)M * N * 2))
+        return NC_ERR_INVALID_ARG;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return internal_cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDev) return NC_ERR_INVALID_ARG;
+    int* status = nullptr;
+    int st = internal_status_word(&status);
+    if (st) return st;
+    static bool attr_set[kMaxDev] = {};
+    static int sms[kMaxDev] = {};
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kTSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return internal_cuda_fail(e);
+        attr_set[dev] = true;
+    }
+    CUtensorMap mx, mw;
+    if (!map_2d(&mx, x, M, K, kTBM, dev) || !map_2d(&mw, w, N, K, kTBN, dev))
+        return NC_ERR_INVALID_ARG;
+    TileParams p;
+    p.out = static_cast<bf16*>(out);
+    p.x = static_cast<const bf16*>(x);
+    p.residual = static_cast<const bf16*>(residual);
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.kb_total = (K + kTileK - 1) / kTileK;
+    p.m_tiles = (M + kTBM - 1) / kTBM;
+    p.n_tiles = (N + kTBN - 1) / kTBN;
+    p.tiles = p.m_tiles * p.n_tiles;
+    // With at most one row block per SM, each CTA keeps a row block (its RMSNorm scales are
+    // computed once) and the grid is a whole number of CTAs per row block.
+    p.n_per = p.m_tiles <= sms[dev] ? std::min(p.n_tiles, sms[dev] / p.m_tiles) : 0;
+    p.flags = flags;
+    p.cap = cap;
+    p.seg_cols = seg_cols;
+    p.status = status;
+    const unsigned grid =
+        (unsigned)(p.n_per ? p.m_tiles * p.n_per : std::min(p.tiles, sms[dev]));
+    gemm_tile_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(mx, mw, p);
+    e = cudaGetLastError();
     return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }
 

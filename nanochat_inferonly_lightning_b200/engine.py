@@ -19,10 +19,12 @@ What runs where:
   per-row scale applied inside them.  A decode layer is four GEMM launches and one attention
   launch; the step starts with one embedding-gather + RMSNorm launch and ends with an argmax
   launch on the device (gemm.py);
-* the prompt pass (all sequences' B*P rows together; `admit` runs one sequence) with its GEMMs
-  on cuBLAS through torch (fp32 accumulation; product + residual rounded once) and the
-  parameter-free RMSNorm, ReLU^2, tanh cap and embedding gather as torch operations, its
-  attention on this library (RoPE/QK-norm/append pass and the batched tcgen05 prefill).
+* the prompt pass (all sequences' B*P rows together; `admit` runs one sequence) on this library
+  too: the embedding gather + RMSNorm kernel, the prompt-pass tcgen05 GEMM (nc_gemm) with the
+  same fused steps as the decode step (RMSNorm row scale for Q/K/V and the MLP up projection,
+  ReLU^2, the residual added in place), the attention's RoPE/QK-norm/append pass and batched
+  tcgen05 prefill, and for the last position of each sequence the LM head on the skinny GEMM
+  with the final RMSNorm and tanh cap fused, then the device argmax.
 
 A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
 and replayed; the device length array advances inside the graph.  The reference engine runs one
@@ -43,7 +45,6 @@ N_EMBD = N_HEAD * HEAD_DIM   # 2176
 MLP_HIDDEN = 4 * N_EMBD      # 8704
 VOCAB = 65536
 LOGIT_CAP = 15.0
-NORM_EPS = 1e-6
 SCALE = 1.0 / math.sqrt(HEAD_DIM)
 
 
@@ -64,18 +65,6 @@ class Weights:
                                     v=rnd(N_EMBD, N_EMBD), o=rnd(N_EMBD, N_EMBD),
                                     up=rnd(MLP_HIDDEN, N_EMBD), down=rnd(N_EMBD, MLP_HIDDEN)))
         self.lm_head = rnd(VOCAB, N_EMBD)
-
-
-def rmsnorm(x):
-    """Parameter-free RMSNorm in fp32 (kernels/rmsnorm.cu: x * rsqrt(mean(x^2) + 1e-6))."""
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + NORM_EPS)).to(torch.bfloat16)
-
-
-def logits_of(w, x):
-    """Final RMSNorm, LM head, tanh soft cap (src/model.cpp:147-155)."""
-    lg = (rmsnorm(x) @ w.lm_head.t()).float()
-    return (LOGIT_CAP * torch.tanh(lg / LOGIT_CAP)).to(torch.bfloat16)
 
 
 class BatchedEngine:
@@ -146,22 +135,46 @@ class BatchedEngine:
                               self.kv_len, N_HEAD, SCALE, self.max_len, self.ws, overlap=True)
 
     # ------------------------------------------------------------------ prompt
+    def _prompt_layers(self, tokens, attention):
+        """The prompt pass's layers over rows = tokens (int64 [R]); attention(i, q, k, v, a)
+        runs layer i's attention.  Returns the residual stream [R, N_EMBD] after the last
+        layer.  Per layer (src/model.cpp:101-154): Q/K/V from RMSNorm(x) in one GEMM pass,
+        attention, output projection + residual in place, MLP up from RMSNorm(x) with ReLU^2,
+        MLP down + residual in place."""
+        w = self.w
+        R = int(tokens.numel())
+        bf = dict(dtype=torch.bfloat16, device=tokens.device)
+        x = torch.empty((R, N_EMBD), **bf)
+        G.embed_rmsnorm(x, w.embed, tokens.to(torch.int32))  # embedding + RMSNorm (:158-162)
+        qkv = torch.empty((3, R, N_EMBD), **bf)
+        a = torch.empty((R, N_EMBD), **bf)
+        h = torch.empty((R, MLP_HIDDEN), **bf)
+        for i, l in enumerate(w.layers):
+            G.gemm(qkv, x, self.wqkv[i], flags=G.NORM_INPUT, seg_cols=N_EMBD)
+            attention(i, qkv[0], qkv[1], qkv[2], a)
+            G.gemm(x, a, l["o"], residual=x)
+            G.gemm(h, x, l["up"], flags=G.NORM_INPUT | G.RELU2)
+            G.gemm(x, h, l["down"], residual=x)
+        return x
+
+    def _first_tokens(self, last):
+        """Greedy first token of each row of `last` [B, N_EMBD]: final RMSNorm, LM head and
+        tanh cap (src/model.cpp:170-177) on the skinny GEMM, then the device argmax."""
+        logits = torch.empty((last.shape[0], VOCAB), dtype=torch.bfloat16, device=last.device)
+        G.gemm_skinny(logits, last.contiguous(), self.w.lm_head, flags=G.NORM_INPUT | G.TANH_CAP,
+                      cap=LOGIT_CAP)
+        first = torch.empty(last.shape[0], dtype=torch.int32, device=last.device)
+        G.argmax_rows(first, logits)
+        return first
+
     def _prompt_pass(self, b, prompt):
         """Prompt pass of one sequence into slot b's caches (rows [0, P)); returns its first
         generated token (greedy, as the reference's first step, src/engine.cpp:37-62)."""
         P = int(prompt.numel())
         assert 0 < P < self.max_len
-        w = self.w
-        x = rmsnorm(w.embed[prompt])
-        for i, l in enumerate(w.layers):
-            xn = rmsnorm(x)
-            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
-            a = torch.empty_like(q)
-            self._prompt_attention(i, b, q, k, v, P, a)
-            x = torch.addmm(x, a, l["o"].t())
-            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
-            x = torch.addmm(x, h, l["down"].t())
-        return torch.argmax(logits_of(w, x[-1:])[0].float())
+        x = self._prompt_layers(prompt.reshape(-1),
+                                lambda i, q, k, v, a: self._prompt_attention(i, b, q, k, v, P, a))
+        return self._first_tokens(x[-1:])[0]
 
     def prefill(self, prompts):
         """prompts: int64 [B, P] token ids; fills the caches of every slot and sets the first
@@ -171,18 +184,9 @@ class BatchedEngine:
         attention launch covers every sequence."""
         B, P = prompts.shape
         assert B == self.B and P < self.max_len
-        w = self.w
-        x = rmsnorm(w.embed[prompts.reshape(-1)])  # [B*P, N_EMBD]
-        for i, l in enumerate(w.layers):
-            xn = rmsnorm(x)
-            q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
-            a = torch.empty_like(q)
-            self._prompt_attention_all(i, q, k, v, P, a)
-            x = torch.addmm(x, a, l["o"].t())
-            h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
-            x = torch.addmm(x, h, l["down"].t())
-        last = x.view(B, P, N_EMBD)[:, -1]
-        first = torch.argmax(logits_of(w, last).float(), dim=-1)
+        x = self._prompt_layers(prompts.reshape(-1),
+                                lambda i, q, k, v, a: self._prompt_attention_all(i, q, k, v, P, a))
+        first = self._first_tokens(x.view(B, P, N_EMBD)[:, -1])
         self.kv_len.fill_(P)
         self.tok.copy_(first)
         self.active.fill_(1)

@@ -1,4 +1,5 @@
-"""Python mirror of the decode-step GEMM entry point (nc_gemm_skinny) over the C ABI.
+"""Python mirror of the GEMM entry points (nc_gemm_skinny for the decode step, nc_gemm for the
+prompt pass) over the C ABI.
 
 out[M, N] = epilogue(x[M, K] . w[N, K]^T) for M <= 64 rows, w in the reference layout W[out, in]
 (src/model.h:30-47), with the RMSNorm that precedes the reference's projections
@@ -42,6 +43,25 @@ def gemm_skinny(out, x, w, residual=None, flags=0, cap=0.0, seg_cols=0, splits=0
     _lib.check("nc_gemm_skinny",
                lib.nc_gemm_skinny(_ptr(out), _ptr(x), _ptr(w), _ptr(residual), M, N, K, flags,
                                   ctypes.c_float(cap), seg_cols, splits, _stream(stream)))
+    return out
+
+
+def gemm(out, x, w, residual=None, flags=0, cap=0.0, seg_cols=0, stream=None):
+    """The same product and fused steps as gemm_skinny for any number of rows, on the
+    persistent tiled kernel (nc_gemm) laid out for the prompt pass."""
+    _bf16(out, x, w, residual)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w is {tuple(w.shape)}, x is {tuple(x.shape)}")
+    if out.numel() != M * N:
+        raise ValueError(f"out has {out.numel()} elements, expected {M * N}")
+    if residual is not None:
+        flags |= RESIDUAL
+    lib = _lib.load()
+    _lib.check("nc_gemm",
+               lib.nc_gemm(_ptr(out), _ptr(x), _ptr(w), _ptr(residual), M, N, K, flags,
+                           ctypes.c_float(cap), seg_cols, _stream(stream)))
     return out
 
 

@@ -37,24 +37,37 @@ def setup():
     assert nc.device_status(reset=True) == 0, "a kernel's bounded wait gave up"
 
 
+def rmsnorm(x):
+    """Parameter-free RMSNorm in fp32 (kernels/rmsnorm.cu: x * rsqrt(mean(x^2) + 1e-6))."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+
+def logits_of(w, x, cap=15.0):
+    """Final RMSNorm, LM head, tanh soft cap (src/model.cpp:147-155)."""
+    lg = (rmsnorm(x) @ w.lm_head.t()).float()
+    return (cap * torch.tanh(lg / cap)).to(torch.bfloat16)
+
+
 def full_logits(E, w, seq_tokens):
-    """Last-position logits of one sequence, recomputed through the prefill path."""
+    """Last-position logits of one sequence, recomputed independently of the engine: torch's
+    RMSNorm and cuBLAS GEMMs around this library's prefill attention, over all positions."""
     import nanochat_inferonly_lightning_b200 as nc
 
     P = len(seq_tokens)
     kc = torch.zeros(P, E.N_HEAD, E.HEAD_DIM, dtype=torch.bfloat16, device="cuda")
     vc = torch.zeros_like(kc)
-    x = E.rmsnorm(w.embed[torch.tensor(seq_tokens, device="cuda")])
+    x = rmsnorm(w.embed[torch.tensor(seq_tokens, device="cuda")])
     for l in w.layers:
-        xn = E.rmsnorm(x)
+        xn = rmsnorm(x)
         q, k, v = xn @ l["q"].t(), xn @ l["k"].t(), xn @ l["v"].t()
         a = torch.empty_like(q)
         nc.rope_qknorm_append(q, k, v, kc, vc, P, E.N_HEAD, 0)
         nc.flash_attention(a, q, kc, vc, P, P, E.N_HEAD, E.SCALE, 0)
         x = torch.addmm(x, a, l["o"].t())
-        h = torch.relu(E.rmsnorm(x) @ l["up"].t()).square()
+        h = torch.relu(rmsnorm(x) @ l["up"].t()).square()
         x = torch.addmm(x, h, l["down"].t())
-    return E.logits_of(w, x[-1:])[0].float()
+    return logits_of(w, x[-1:])[0].float()
 
 
 def test_graph_replay_matches_eager(setup):
