@@ -154,6 +154,29 @@ int nc_decode_attention_noalloc(void* out, const void* q, const void* k_new, con
                                 int batch, int heads, float scale, int max_kv_len,
                                 cudaStream_t stream);
 
+/* nc_rope_qknorm_append for `batch` sequences in one launch: q, k, v are [batch, seq_len,
+ * heads, 128] (sequence b's chunk at rows b*seq_len..), all at positions start_pos ..
+ * start_pos + seq_len - 1; sequence b's cache starts at k_slab / v_slab + b * seq_stride
+ * elements (seq_stride % 8 == 0 and at least (start_pos + seq_len) * heads * 128 when
+ * batch > 1), the layout nc_prefill_attention_batched reads.
+ * Replaces: the same calls as nc_rope_qknorm_append (src/model.cpp:119-131), once per
+ * sequence of a batched prompt pass. */
+int nc_rope_qknorm_append_batched(void* q, const void* k, const void* v, void* k_slab,
+                                  void* v_slab, long long seq_stride, int batch, int seq_len,
+                                  int heads, int start_pos, cudaStream_t stream);
+
+/* nc_rope_qknorm_append_paged for `batch` sequences in one launch, through a DEVICE page table
+ * [batch][pages_per_seq] (the one nc_prefill_attention_paged / nc_decode_attention_paged read):
+ * q, k, v are [batch, seq_len, heads, 128], all at positions start_pos .. start_pos + seq_len - 1
+ * ((start_pos + seq_len - 1) / page_rows < pages_per_seq).  A page id outside [0, num_pages)
+ * is not written to and sets bit 0x400 of the device status word.  No counterpart in the
+ * reference. */
+int nc_rope_qknorm_append_paged_batched(void* q, const void* k, const void* v, void* k_pool,
+                                        void* v_pool, int num_pages, int page_rows,
+                                        const int* page_table, int pages_per_seq, int batch,
+                                        int seq_len, int heads, int start_pos,
+                                        cudaStream_t stream);
+
 /* Batched causal prefill (chunked, with cache offset) for `batch` sequences whose caches
  * are slices of one slab: sequence b's rows start at k_slab + b * seq_stride elements
  * (seq_stride >= rows_per_seq * heads * 128).  Sequence b's chunk of seq_q queries sits at

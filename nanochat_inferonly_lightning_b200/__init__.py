@@ -10,12 +10,13 @@ from . import gemm
 from .attn import (HEAD_DIM, ROPE_MAX_SEQ, KVCache, apply_rope, apply_rope_rmsnorm,
                    decode_attention, decode_attention_paged, decode_workspace_bytes, device_status, flash_attention,
                    init_rope_tables, prefill_attention_batched, prefill_attention_paged,
-                   rope_qknorm_append, rope_qknorm_append_paged)
+                   rope_qknorm_append, rope_qknorm_append_batched, rope_qknorm_append_paged,
+                   rope_qknorm_append_paged_batched)
 
 __all__ = [
     "LIB_PATH", "NcError", "load", "HEAD_DIM", "ROPE_MAX_SEQ", "KVCache", "apply_rope",
     "apply_rope_rmsnorm", "decode_attention", "decode_attention_paged", "decode_workspace_bytes", "device_status",
     "flash_attention", "init_rope_tables", "prefill_attention_batched", "prefill_attention_paged", "rope_qknorm_append",
-    "rope_qknorm_append_paged",
+    "rope_qknorm_append_batched", "rope_qknorm_append_paged", "rope_qknorm_append_paged_batched",
     "gemm",
 ]

@@ -41,6 +41,12 @@ SIGNATURES = {
     "nc_decode_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p, c_int, c_int, c_float, c_int,
                                             c_void_p]),
+    "nc_rope_qknorm_append_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_void_p, c_longlong, c_int, c_int, c_int, c_int,
+                                              c_void_p]),
+    "nc_rope_qknorm_append_paged_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                                    c_void_p, c_int, c_int, c_void_p, c_int,
+                                                    c_int, c_int, c_int, c_int, c_void_p]),
     "nc_prefill_attention_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
                                              c_longlong, c_int, c_void_p, c_int, c_int, c_int,
                                              c_float, c_void_p]),

@@ -72,6 +72,19 @@ def rope_qknorm_append(q, k, v, k_cache, v_cache, seq_len, heads, start_pos, str
                                          seq_len, heads, start_pos, _stream(stream)))
 
 
+def rope_qknorm_append_batched(q, k, v, k_slab, v_slab, seq_stride, batch, seq_len, heads,
+                               start_pos, stream=None):
+    """nc_rope_qknorm_append_batched: rope_qknorm_append for `batch` sequences in one launch.
+    q, k, v are [batch * seq_len, heads, 128]; sequence b's cache starts seq_stride elements
+    after sequence b-1's in k_slab / v_slab."""
+    _bf16(q, k, v, k_slab, v_slab)
+    lib = _lib.load()
+    _lib.check("nc_rope_qknorm_append_batched",
+               lib.nc_rope_qknorm_append_batched(_ptr(q), _ptr(k), _ptr(v), _ptr(k_slab),
+                                                 _ptr(v_slab), int(seq_stride), batch, seq_len,
+                                                 heads, start_pos, _stream(stream)))
+
+
 def flash_attention(out, Q, K, V, seq_q, kv_len, heads, scale, kv_offset, stream=None):
     """kernels/flash_attention.cu:159-171: causal attention of Q [seq_q, heads, 128] over the
     cache K/V [>= kv_len, heads, 128]; key j is visible to query s iff j < kv_len and
@@ -143,6 +156,22 @@ def rope_qknorm_append_paged(q, k, v, k_pool, v_pool, pages, seq_len, heads, sta
                                                _ptr(v_pool), int(k_pool.shape[0]),
                                                int(k_pool.shape[1]), ids, len(pages), seq_len,
                                                heads, start_pos, _stream(stream)))
+
+
+def rope_qknorm_append_paged_batched(q, k, v, k_pool, v_pool, page_table, seq_len, heads,
+                                     start_pos, stream=None):
+    """nc_rope_qknorm_append_paged_batched: rope_qknorm_append_paged for every row of the device
+    page table (int32 CUDA [B, pages_per_seq]) in one launch; q, k, v are [B * seq_len, heads,
+    128]."""
+    _bf16(q, k, v, k_pool, v_pool)
+    if page_table.dtype != torch.int32 or not page_table.is_cuda or not page_table.is_contiguous():
+        raise ValueError("page_table must be a contiguous int32 CUDA tensor")
+    lib = _lib.load()
+    _lib.check("nc_rope_qknorm_append_paged_batched",
+               lib.nc_rope_qknorm_append_paged_batched(
+                   _ptr(q), _ptr(k), _ptr(v), _ptr(k_pool), _ptr(v_pool), int(k_pool.shape[0]),
+                   int(k_pool.shape[1]), _ptr(page_table), int(page_table.shape[1]),
+                   int(page_table.shape[0]), seq_len, heads, start_pos, _stream(stream)))
 
 
 def prefill_attention_paged(out, q, k_pool, v_pool, page_table, kv_offset, seq_q, heads, scale,

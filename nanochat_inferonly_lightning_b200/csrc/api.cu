@@ -522,6 +522,73 @@ int nc_rope_qknorm_append_paged(void* q, const void* k, const void* v, void* k_p
     return NC_OK;
 }
 
+int nc_rope_qknorm_append_batched(void* q, const void* k, const void* v, void* k_slab,
+                                  void* v_slab, long long seq_stride, int batch, int seq_len,
+                                  int heads, int start_pos, cudaStream_t stream) {
+    if (batch < 0 || seq_len < 0 || start_pos < 0 || check_heads(heads)) return NC_ERR_INVALID_ARG;
+    if (batch == 0 || seq_len == 0) return NC_OK;
+    if (!q || !k || !v || !k_slab || !v_slab) return NC_ERR_INVALID_ARG;
+    if (seq_stride % 8 || (batch > 1 && seq_stride < (long long)(start_pos + seq_len) * heads * kHeadDim))
+        return NC_ERR_INVALID_ARG;
+    if ((long long)batch * seq_len * heads > INT32_MAX / 2) return NC_ERR_INVALID_ARG;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_slab) || !aligned16(v_slab))
+        return NC_ERR_MISALIGNED;
+    if ((long long)start_pos + seq_len > kRopeMaxSeq) return NC_ERR_RANGE;
+    RopeArgs a{};
+    int st = ensure_rope(&a.rope_cs);
+    if (st) return st;
+    const size_t row0 = (size_t)start_pos * heads * kHeadDim;
+    a.q = static_cast<bf16*>(q);
+    a.k = static_cast<const bf16*>(k);
+    a.v = static_cast<const bf16*>(v);
+    a.k_dst = static_cast<bf16*>(k_slab) + row0;
+    a.v_dst = static_cast<bf16*>(v_slab) + row0;
+    a.seq_len = seq_len;
+    a.heads = heads;
+    a.start_pos = start_pos;
+    a.batch = batch;
+    a.dst_stride = seq_stride;
+    cudaError_t e = launch_rope(kRopeNormAppend, a, stream);
+    return e == cudaSuccess ? NC_OK : cuda_fail(e);
+}
+
+int nc_rope_qknorm_append_paged_batched(void* q, const void* k, const void* v, void* k_pool,
+                                        void* v_pool, int num_pages, int page_rows,
+                                        const int* page_table, int pages_per_seq, int batch,
+                                        int seq_len, int heads, int start_pos,
+                                        cudaStream_t stream) {
+    if (batch < 0 || seq_len < 0 || start_pos < 0 || check_heads(heads)) return NC_ERR_INVALID_ARG;
+    if (batch == 0 || seq_len == 0) return NC_OK;
+    if (!q || !k || !v || !k_pool || !v_pool || !page_table || page_rows < 1 || num_pages < 1)
+        return NC_ERR_INVALID_ARG;
+    if ((long long)(start_pos + seq_len - 1) / page_rows >= pages_per_seq) return NC_ERR_INVALID_ARG;
+    if ((long long)batch * seq_len * heads > INT32_MAX / 2) return NC_ERR_INVALID_ARG;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_pool) ||
+        !aligned16(v_pool))
+        return NC_ERR_MISALIGNED;
+    if ((long long)start_pos + seq_len > kRopeMaxSeq) return NC_ERR_RANGE;
+    RopeArgs a{};
+    int st = ensure_rope(&a.rope_cs);
+    if (st) return st;
+    st = status_word(&a.status);
+    if (st) return st;
+    a.q = static_cast<bf16*>(q);
+    a.k = static_cast<const bf16*>(k);
+    a.v = static_cast<const bf16*>(v);
+    a.k_dst = static_cast<bf16*>(k_pool);
+    a.v_dst = static_cast<bf16*>(v_pool);
+    a.seq_len = seq_len;
+    a.heads = heads;
+    a.start_pos = start_pos;
+    a.batch = batch;
+    a.page_table = page_table;
+    a.pages_per_seq = pages_per_seq;
+    a.page_rows = page_rows;
+    a.num_pages = num_pages;
+    cudaError_t e = launch_rope(kRopeNormAppend, a, stream);
+    return e == cudaSuccess ? NC_OK : cuda_fail(e);
+}
+
 int nc_prefill_attention_batched(void* out, const void* q, const void* k_slab,
                                  const void* v_slab, long long seq_stride, int rows_per_seq,
                                  const int* kv_offset, int batch, int seq_q, int heads,

@@ -182,6 +182,17 @@ struct RopeArgs {
     int seq_len;
     int heads;
     int start_pos;
+    // Append mode over several sequences: q, k, v hold batch x seq_len rows, sequence b's
+    // rows go to k_dst / v_dst + b * dst_stride elements (its cache, from row start_pos).
+    int batch = 1;
+    long long dst_stride = 0;
+    // Paged destination (page_table != null): k_dst / v_dst are pools
+    // [num_pages][page_rows][heads][128]; position p of sequence b goes to row p % page_rows of
+    // page page_table[b * pages_per_seq + p / page_rows].  A page id outside [0, num_pages) ORs
+    // 0x400 into *status and the row is not written.
+    const int* page_table = nullptr;
+    int pages_per_seq = 0, page_rows = 0, num_pages = 0;
+    int* status = nullptr;
 };
 
 cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream);

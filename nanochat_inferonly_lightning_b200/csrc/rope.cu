@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "nc_common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace nc {
 
@@ -97,6 +98,22 @@ __device__ __forceinline__ void rope_norm_pairs(const float4 (&cs)[4], uint4 lo,
     out_hi = f32_to_bf16x8(yh);
 }
 
+// Element offset of row `row` (lane slice s8) in k_dst / v_dst: sequence row / rps at its row
+// row % rps from start_pos, in a contiguous slot (dst_stride apart) or through the page table.
+// -1 when the page id is out of range (recorded in the status word).
+__device__ __forceinline__ long long dst_offset(const RopeArgs& a, int row, int rps, int s8) {
+    const int b = row / rps, r = row % rps;
+    if (!a.page_table) return (long long)b * a.dst_stride + (long long)r * kHeadDim + 8 * s8;
+    const int pos = a.start_pos + r / a.heads;
+    const int page = a.page_table[(size_t)b * a.pages_per_seq + pos / a.page_rows];
+    if (page < 0 || page >= a.num_pages) {
+        if (s8 == 0) atomicOr(a.status, kStatusBounds);
+        return -1;
+    }
+    return (((long long)page * a.page_rows + pos % a.page_rows) * a.heads + r % a.heads) * kHeadDim +
+           8 * s8;
+}
+
 // Persistent, grid-stride streaming pass: each 8-lane group walks rows row, row + stride,
 // ... and issues the loads of its next row (data and cos/sin) before it computes the
 // current one.  Raw inputs
@@ -112,15 +129,18 @@ __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
     const int stride = (gridDim.x * kRopeThreads) >> 3;
     const int s8 = threadIdx.x & 7;
     const unsigned gmask = 0xFFu << (threadIdx.x & 24);
-    const int nrows = a.seq_len * a.heads;
+    const int rps = a.seq_len * a.heads;  // rows per sequence
+    const int nrows = rps * a.batch;
     int row = grp;
     if (row >= nrows) return;  // whole 8-lane groups leave together
-    RowIn cur = load_row<MODE>(a, (size_t)row * kHeadDim + 8 * s8, a.start_pos + row / a.heads, s8);
+    RowIn cur = load_row<MODE>(a, (size_t)row * kHeadDim + 8 * s8,
+                               a.start_pos + (row % rps) / a.heads, s8);
     for (; row < nrows; row += stride) {
         const int next = row + stride;
         RowIn nxt;
         if (next < nrows)
-            nxt = load_row<MODE>(a, (size_t)next * kHeadDim + 8 * s8, a.start_pos + next / a.heads, s8);
+            nxt = load_row<MODE>(a, (size_t)next * kHeadDim + 8 * s8,
+                                 a.start_pos + (next % rps) / a.heads, s8);
         const size_t off = (size_t)row * kHeadDim + 8 * s8;
         uint4 ol, oh;
         if (MODE == kRopeNormAppend) {
@@ -128,10 +148,13 @@ __global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(RopeArgs a) {
             *reinterpret_cast<uint4*>(a.q + off) = ol;
             *reinterpret_cast<uint4*>(a.q + off + 64) = oh;
             rope_norm_pairs(cur.cs, cur.klo, cur.khi, gmask, true, ol, oh);
-            *reinterpret_cast<uint4*>(a.k_dst + off) = ol;
-            *reinterpret_cast<uint4*>(a.k_dst + off + 64) = oh;
-            *reinterpret_cast<uint4*>(a.v_dst + off) = cur.vlo;
-            *reinterpret_cast<uint4*>(a.v_dst + off + 64) = cur.vhi;
+            const long long doff = dst_offset(a, row, rps, s8);
+            if (doff >= 0) {
+                *reinterpret_cast<uint4*>(a.k_dst + doff) = ol;
+                *reinterpret_cast<uint4*>(a.k_dst + doff + 64) = oh;
+                *reinterpret_cast<uint4*>(a.v_dst + doff) = cur.vlo;
+                *reinterpret_cast<uint4*>(a.v_dst + doff + 64) = cur.vhi;
+            }
         } else {
             rope_norm_pairs(cur.cs, cur.qlo, cur.qhi, gmask, MODE == kRopeNorm, ol, oh);
             *reinterpret_cast<uint4*>(a.q + off) = ol;
@@ -164,7 +187,7 @@ cudaError_t launch_rope_mode(const RopeArgs& a, long long rows, int dev, cudaStr
 }  // namespace
 
 cudaError_t launch_rope(RopeMode mode, const RopeArgs& a, cudaStream_t stream) {
-    const long long rows = (long long)a.seq_len * a.heads;
+    const long long rows = (long long)a.seq_len * a.heads * a.batch;
     if (rows <= 0) return cudaSuccess;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

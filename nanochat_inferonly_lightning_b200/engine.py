@@ -8,8 +8,9 @@ LM head, tanh soft cap 15.  Sampling is the reference's greedy rule (src/engine.
 first maximum).  Weights use the reference's layout W[out, in] (src/model.h:30-47).
 
 What runs where:
-* the attention path (the part this library replaces) on this library: for a prompt,
-  nc_rope_qknorm_append + nc_flash_attention per sequence (tcgen05 prefill); for each decode
+* the attention path (the part this library replaces) on this library: for a prompt pass over
+  all slots, one nc_rope_qknorm_append_batched and one nc_prefill_attention_batched per layer
+  (tcgen05 prefill; `admit` of one sequence uses the single-sequence calls); for each decode
   step, one nc_decode_attention over the whole batch (RoPE + QK-norm of q and k, append, and
   split-KV attention in one kernel), reading per-sequence lengths from a device array;
 * the decode step's GEMMs on this library's skinny tcgen05 GEMM (gemm.py, nc_gemm_skinny): one
@@ -22,8 +23,8 @@ What runs where:
 * the prompt pass (all sequences' B*P rows together; `admit` runs one sequence) on this library
   too: the embedding gather + RMSNorm kernel, the prompt-pass tcgen05 GEMM (nc_gemm) with the
   same fused steps as the decode step (RMSNorm row scale for Q/K/V and the MLP up projection,
-  ReLU^2, the residual added in place), the attention's RoPE/QK-norm/append pass and batched
-  tcgen05 prefill, and for the last position of each sequence the LM head on the skinny GEMM
+  ReLU^2, the residual added in place), the attention's batched RoPE/QK-norm/append pass and
+  batched tcgen05 prefill, and for the last position of each sequence the LM head on the skinny GEMM
   with the final RMSNorm and tanh cap fused, then the device argmax.
 
 A decode step has static shapes and no host-side state, so it is captured once in a CUDA graph
@@ -121,12 +122,11 @@ class BatchedEngine:
 
     def _prompt_attention_all(self, i, q, k, v, P, a):
         """Layer i, every slot's prompt of P rows (rows b*P.. of q, k, v)."""
-        for b in range(self.B):
-            r = slice(b * P, (b + 1) * P)
-            attn.rope_qknorm_append(q[r], k[r], v[r], self.k[i][b], self.v[i][b], P, N_HEAD, 0)
+        stride = self.max_len * N_HEAD * HEAD_DIM
+        attn.rope_qknorm_append_batched(q, k, v, self.k[i], self.v[i], stride, self.B, P, N_HEAD, 0)
         offs = torch.zeros(self.B, dtype=torch.int32, device=q.device)
-        attn.prefill_attention_batched(a, q, self.k[i], self.v[i], self.max_len * N_HEAD * HEAD_DIM,
-                                       self.max_len, offs, P, N_HEAD, SCALE)
+        attn.prefill_attention_batched(a, q, self.k[i], self.v[i], stride, self.max_len, offs, P,
+                                       N_HEAD, SCALE)
 
     def _decode_attention(self, i, a, qkv):
         # right after the Q/K/V GEMM, which writes no cache: the attention CTAs may start
@@ -258,8 +258,9 @@ class PagedEngine(BatchedEngine):
     its prompt needs when it is admitted, one more page whenever a decode step is about to write
     the first row of a new page, and takes them all back when the slot retires, so the cache
     holds only the live sequences' rows (num_pages may be far below batch * max_len /
-    page_rows).  The attention calls are the library's paged forms (nc_rope_qknorm_append_paged,
-    nc_prefill_attention_paged, nc_decode_attention_paged); everything else is BatchedEngine's.
+    page_rows).  The attention calls are the library's paged forms (nc_rope_qknorm_append_paged and
+    its batched form over the device page table, nc_prefill_attention_paged,
+    nc_decode_attention_paged); everything else is BatchedEngine's.
     A retired slot's length is set to 0, so a decode step reads and writes none of its old pages.
     """
 
@@ -306,10 +307,8 @@ class PagedEngine(BatchedEngine):
                                      P, N_HEAD, SCALE)
 
     def _prompt_attention_all(self, i, q, k, v, P, a):
-        for b in range(self.B):
-            r = slice(b * P, (b + 1) * P)
-            attn.rope_qknorm_append_paged(q[r], k[r], v[r], self.k[i], self.v[i], self.pages[b],
-                                          P, N_HEAD, 0)
+        attn.rope_qknorm_append_paged_batched(q, k, v, self.k[i], self.v[i], self.page_table, P,
+                                              N_HEAD, 0)
         offs = torch.zeros(self.B, dtype=torch.int32, device=q.device)
         attn.prefill_attention_paged(a, q, self.k[i], self.v[i], self.page_table, offs, P,
                                      N_HEAD, SCALE)

@@ -141,6 +141,38 @@ def test_rope_qknorm_append(nc, seq_len, start_pos):
     assert np.array_equal(bf16_to_u16(tkc)[start_pos + seq_len:], kc0[start_pos + seq_len:])
 
 
+@pytest.mark.parametrize("batch,seq_len,start_pos", [(1, 3, 0), (3, 37, 0), (8, 64, 100)])
+def test_rope_qknorm_append_batched(nc, batch, seq_len, start_pos):
+    """One launch over `batch` sequences equals `batch` single-sequence appends (the oracle per
+    sequence): each chunk lands in its own cache slot, rows outside the window untouched."""
+    slot_rows = start_pos + seq_len + 5
+    q = randn_u16((batch * seq_len, H, D), 40)
+    k = randn_u16((batch * seq_len, H, D), 41)
+    v = randn_u16((batch * seq_len, H, D), 42)
+    kc0 = randn_u16((batch, slot_rows, H, D), 43)
+    vc0 = randn_u16((batch, slot_rows, H, D), 44)
+    tq, tk, tv, tkc, tvc = dev(q), dev(k), dev(v), dev(kc0), dev(vc0)
+    nc.rope_qknorm_append_batched(tq, tk, tv, tkc, tvc, slot_rows * H * D, batch, seq_len, H,
+                                  start_pos)
+    gq, gkc, gvc = bf16_to_u16(tq), bf16_to_u16(tkc), bf16_to_u16(tvc)
+    for b in range(batch):
+        r = slice(b * seq_len, (b + 1) * seq_len)
+        wq, wkc, wvc = oracle.rope_qknorm_append(q[r], k[r], v[r], kc0[b], vc0[b], seq_len, H,
+                                                 start_pos)
+        assert ulp_diff_bf16(gq[r], wq).max() <= 1
+        assert ulp_diff_bf16(gkc[b], wkc).max() <= 1
+        assert np.array_equal(gvc[b], wvc)
+        assert np.array_equal(gkc[b][:start_pos], kc0[b][:start_pos])
+        assert np.array_equal(gkc[b][start_pos + seq_len:], kc0[b][start_pos + seq_len:])
+
+
+def test_rope_qknorm_append_batched_rejects_short_stride(nc):
+    t = dev(randn_u16((2 * 4, H, D), 45))
+    c = dev(randn_u16((2, 4, H, D), 46))
+    with pytest.raises(RuntimeError):
+        nc.rope_qknorm_append_batched(t, t.clone(), t.clone(), c, c.clone(), 3 * H * D, 2, 4, H, 0)
+
+
 # ----------------------------------------------------------------------------- prefill
 PREFILL_CASES = [
     # (seq_q, kv_len, kv_offset)
@@ -476,6 +508,56 @@ def test_prefill_paged(nc, offs, chunk, page_rows):
         assert np.array_equal(got_v, wvs[b][off:off + chunk])
         assert_close_bf16(bf16_to_u16(out[b]), wants[b], what=f"paged prefill seq {b}")
     assert nc.device_status(reset=True) == 0
+
+
+@pytest.mark.parametrize("B,chunk,start,page_rows", [(3, 200, 100, 128), (8, 64, 0, 16)])
+def test_rope_qknorm_append_paged_batched(nc, B, chunk, start, page_rows):
+    """One launch for every sequence of a device page table (shuffled pages, chunks crossing
+    page edges) equals the oracle's append per sequence; the row of a sequence whose page id is
+    out of range is skipped and reported in the status word."""
+    pps = -(-(start + chunk) // page_rows)
+    num_pages = B * pps + 3
+    rng = np.random.default_rng(900 + page_rows)
+    table = rng.permutation(num_pages).astype(np.int32)[:B * pps].reshape(B, pps)
+    kpool0 = randn_u16((num_pages, page_rows, H, D), 901)
+    vpool0 = randn_u16((num_pages, page_rows, H, D), 902)
+    q = randn_u16((B * chunk, H, D), 903)
+    k = randn_u16((B * chunk, H, D), 904)
+    v = randn_u16((B * chunk, H, D), 905)
+    tk, tv, tq = dev(kpool0), dev(vpool0), dev(q)
+    nc.rope_qknorm_append_paged_batched(tq, dev(k), dev(v), tk, tv,
+                                        torch.tensor(table, device="cuda"), chunk, H, start)
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) == 0
+    gq, gk, gv = bf16_to_u16(tq), bf16_to_u16(tk), bf16_to_u16(tv)
+    rows = np.arange(start, start + chunk)
+    touched = np.zeros((num_pages, page_rows), bool)
+    for b in range(B):
+        r = slice(b * chunk, (b + 1) * chunk)
+        kc = np.zeros((start + chunk, H, D), np.uint16)
+        vc = np.zeros_like(kc)
+        wq, wkc, wvc = oracle.rope_qknorm_append(q[r], k[r], v[r], kc, vc, chunk, H, start)
+        assert ulp_diff_bf16(gq[r], wq).max() <= 1
+        pg, pr = table[b, rows // page_rows], rows % page_rows
+        assert ulp_diff_bf16(gk[pg, pr], wkc[start:]).max() <= 1
+        assert np.array_equal(gv[pg, pr], wvc[start:])
+        touched[pg, pr] = True
+    assert np.array_equal(gk[~touched], kpool0[~touched])
+    assert np.array_equal(gv[~touched], vpool0[~touched])
+
+    # a page id outside [0, num_pages): that sequence's rows on the page are not written
+    bad = table.copy()
+    bad[0, -1] = num_pages
+    tk2, tv2 = dev(kpool0), dev(vpool0)
+    nc.rope_qknorm_append_paged_batched(dev(q), dev(k), dev(v), tk2, tv2,
+                                        torch.tensor(bad, device="cuda"), chunk, H, start)
+    torch.cuda.synchronize()
+    assert nc.device_status(reset=True) & 0x400
+    g2 = bf16_to_u16(tk2)
+    in_bad = rows // page_rows == pps - 1
+    assert np.array_equal(g2[table[0, -1]], kpool0[table[0, -1]])
+    assert np.array_equal(g2[bad[0, rows[~in_bad] // page_rows], rows[~in_bad] % page_rows],
+                          gk[bad[0, rows[~in_bad] // page_rows], rows[~in_bad] % page_rows])
 
 
 # ----------------------------------------------------------------------------- KV cache object
