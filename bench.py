@@ -705,6 +705,54 @@ def bench_gemm(dist, stepper, K, Wm, peaks, traffic, M=8):
     return out
 
 
+def bench_prompt_gemm(dist, stepper, K, Wm, peaks, M=2048, shapes=None):
+    """The prompt-pass tcgen05 GEMM (nc_gemm) on the four per-layer shapes of the cfg5 prompt
+    pass (8 sequences x 256 tokens = 2048 rows) with their fused steps.  Each step runs one
+    call per input set, over enough sets (x, weight, out; > 2x L2 together) that every call
+    reads its operands from HBM, from one CUDA graph replay.  FLOPs per call: 2*M*N*K."""
+    import nanochat_inferonly_lightning_b200 as nc
+
+    G = nc.gemm
+    out = {}
+    for name, N, Kd, flag_names, seg in (shapes or GEMM_SHAPES[:4]):
+        flags = 0
+        for f in flag_names.split("|"):
+            flags |= getattr(G, f)
+        per_set = (N * Kd + M * Kd + M * N) * 2
+        sets = max(2, -(-int(2.2 * L2_BYTES) // per_set))
+        g = torch.Generator(device="cuda").manual_seed(60 + dist.rank)
+        data = [((torch.randn((M, Kd), generator=g, device="cuda")).to(torch.bfloat16),
+                 (torch.randn((N, Kd), generator=g, device="cuda") * 0.02).to(torch.bfloat16),
+                 torch.randn((M, N), generator=g, device="cuda").to(torch.bfloat16))
+                for _ in range(sets)]
+
+        def calls():
+            for x, w, y in data:
+                # the residual flag adds y in place (out == residual), as the engine does
+                G.gemm(y, x, w, residual=y if flags & G.RESIDUAL else None,
+                       flags=flags & ~G.RESIDUAL, cap=15.0, seg_cols=seg)
+
+        calls()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                calls()
+        torch.cuda.current_stream().wait_stream(side)
+        t_ms = dist.max(stepper.run(graph.replay, K, Wm)) / sets
+        del graph
+        tf = 2.0 * M * N * Kd / (t_ms * 1e-3) / 1e12
+        out[name] = {"M": M, "N": N, "K": Kd, "fused": flag_names, "us": t_ms * 1e3,
+                     "TFLOP_per_s": tf, "frac_bf16": tf / peaks["tflops"]}
+        del data
+        torch.cuda.empty_cache()
+    out["peak_src"] = peaks["src"]
+    out["timing"] = ("mean per call: K replays of a CUDA graph of one call per input set, back "
+                     "to back between two CUDA events; input sets > 2x L2 together")
+    return out
+
+
 def bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic):
     a, b = W.shard(W.CFG4_BATCH, dist.rank, dist.world)
     n = b - a
@@ -795,7 +843,8 @@ def main():
     ap.add_argument("--clock-log-dir", default=None,
                     help="directory for the raw nvidia-smi clock samples (default: the system "
                          "temporary directory)")
-    ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4", "gemm", "cfg5"],
+    ap.add_argument("--only", choices=["prefill", "cfg1", "cfg3", "cfg4", "gemm", "prompt_gemm",
+                                       "cfg5"],
                     default=None,
                     help="run one workload only (profiling); implies --no-cpu, no e2e")
     args = ap.parse_args()
@@ -822,6 +871,7 @@ def main():
                                            W.cfg3_kv_lens(), "cfg3"),
               "cfg4": lambda: bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic),
               "gemm": lambda: bench_gemm(dist, stepper, K, Wm, peaks, traffic),
+              "prompt_gemm": lambda: bench_prompt_gemm(dist, stepper, K, Wm, peaks),
               "cfg5": (lambda: bench_cfg5(dist)) if impl.kind == "nc"
                       else (lambda: bench_cfg5_reference(dist))}[args.only]
         r = fn()
@@ -842,6 +892,7 @@ def main():
         extra["cfg4_chunked_prefill"] = bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic)
         if impl.kind == "nc":
             extra["decode_step_gemms"] = bench_gemm(dist, stepper, K, Wm, peaks, traffic)
+            extra["prompt_pass_gemms"] = bench_prompt_gemm(dist, stepper, K, Wm, peaks)
             extra["cfg5_e2e_generation"] = bench_cfg5(dist)
         else:
             extra["cfg5_e2e_generation"] = bench_cfg5_reference(dist)
