@@ -514,7 +514,8 @@ def bench_cfg5(dist):
     residual, the MLP up projection (RMSNorm, ReLU^2 fused) and down projection + residual on
     the skinny tcgen05 GEMM, then the LM head (RMSNorm, tanh cap fused), with the embedding
     gather + RMSNorm and the argmax as library kernels too.  The prompt pass runs eagerly for
-    all 8 sequences together (cuBLAS GEMMs, this library's attention).  Reported: decode tokens
+    all 8 sequences together, also all on this library (the prompt-pass tcgen05 GEMM nc_gemm,
+    the batched RoPE/append pass and the batched prefill attention).  Reported: decode tokens
     per second (whole job), timed with CUDA events over the 256 steps, and the prompt pass time
     (after one untimed warm-up pass)."""
     from nanochat_inferonly_lightning_b200 import engine as E
