@@ -595,6 +595,298 @@ __global__ void __launch_bounds__(kTThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------
+// nc_gemm on CTA pairs (cta_group::2).  The two CTAs of a cluster share 256 x 256 output
+// tiles: each CTA stages its own 128 rows of x and 128 of the tile's 256 weight rows (16 KB
+// each per 64-deep K block, no multicast), the even CTA issues one M = 256, N = 256 MMA per 16
+// K-elements that reads both CTAs' halves, and each CTA's tensor memory receives its own 128
+// rows of the accumulator.  Per SM that is 32 KB staged from L2 per 512 cycles of MMAs,
+// against 48 KB for a CTA alone on 128 x 256 tiles.
+//   warp 0      TMA producer of each CTA; the loads of both CTAs count on the even CTA's full
+//               barrier (which expects both halves); each CTA waits on its own empty barrier.
+//   warp 1      the even CTA's MMA issuer: commits every stage's release, and each
+//               accumulator's completion, to the barriers of both CTAs.
+//   warps 2-5   epilogue of each CTA on its own 128 rows (as in gemm_tile_kernel); each warp
+//               releases an accumulator buffer with one arrival on the even CTA's barrier.
+// ---------------------------------------------------------------------------------------
+constexpr int kPStages = 6;
+constexpr int kPABytes = kTBM * kTileK * 2;        // 16 KB: this CTA's 128 rows of x
+constexpr int kPBBytes = (kTBN / 2) * kTileK * 2;  // 16 KB: this CTA's 128 rows of w
+
+struct PairTail {
+    uint64_t full[kPStages];   // even CTA: both CTAs' copies of a stage landed (64 KB)
+    uint64_t empty[kPStages];  // each CTA: the MMAs reading its copy of the stage are done
+    uint64_t acc_full[2];      // each CTA: accumulator buffer complete
+    uint64_t acc_empty[2];     // even CTA: all eight epilogue warps read the buffer
+    uint64_t drain;
+    float rs[kTBM];
+    uint32_t tmem;
+    int abort;
+};
+constexpr int kPSmemBytes = kPStages * (kPABytes + kPBBytes) + (int)sizeof(PairTail) + 1024;
+static_assert(kPSmemBytes <= 227 * 1024, "shared memory budget");
+
+// The tiles of one CTA pair, in order; m_tiles counts 256-row blocks.
+struct PairWalk {
+    int mt, nt, t;
+    __device__ __forceinline__ void start(const TileParams& p) {
+        const int pid = blockIdx.x >> 1;
+        if (p.n_per) {
+            mt = pid % p.m_tiles;
+            nt = pid / p.m_tiles;
+        } else {
+            t = pid;
+            mt = t % p.m_tiles;
+            nt = t / p.m_tiles;
+        }
+    }
+    __device__ __forceinline__ bool valid(const TileParams& p) const {
+        return p.n_per ? nt < p.n_tiles : t < p.tiles;
+    }
+    __device__ __forceinline__ void next(const TileParams& p) {
+        if (p.n_per) {
+            nt += p.n_per;
+        } else {
+            t += gridDim.x >> 1;
+            mt = t % p.m_tiles;
+            nt = t / p.m_tiles;
+        }
+    }
+};
+
+constexpr int kTagPEmpty = 0x61, kTagPFull = 0x62, kTagPAccFull = 0x63, kTagPAccEmpty = 0x64,
+              kTagPDrainLoad = 0x65, kTagPDrainMma = 0x66;
+
+__global__ void __launch_bounds__(kTThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const TileParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = base;                          // stage i at sA + i * kPABytes
+    uint8_t* sB = base + kPStages * kPABytes;    // stage i at sB + i * kPBBytes
+    PairTail* tail = reinterpret_cast<PairTail*>(sB + kPStages * kPBBytes);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank() & 1u;  // cluster = one pair
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPStages; ++i) {
+            mbar_init(&tail->full[i], 1);
+            mbar_init(&tail->empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tail->acc_full[i], 1);
+            mbar_init(&tail->acc_empty[i], 8);
+        }
+        mbar_init(&tail->drain, 1);
+        tail->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmX);
+        prefetch_tmap(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&tail->tmem, kTTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    // Both CTAs' barriers are initialised before either signals the other's.
+    cluster_arrive();
+    cluster_wait();
+    tc_fence_after();
+    const uint32_t tmem = tail->tmem;
+    volatile int* abort_flag = &tail->abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int it = 0;  // running k-block count of this pair: stage it % kPStages
+            bool ok = true;
+            PairWalk tw;
+            for (tw.start(p); ok && tw.valid(p); tw.next(p)) {
+                const int m0 = tw.mt * (2 * kTBM) + (int)rank * kTBM;
+                const int n0 = tw.nt * kTBN + (int)rank * (kTBN / 2);
+                for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+                    const int st = it % kPStages;
+                    if (it >= kPStages &&
+                        !(ok = mbar_wait_cl(&tail->empty[st], ((it / kPStages) - 1) & 1,
+                                            abort_flag, p.status, kTagPEmpty)))
+                        break;
+                    const uint32_t full0 = map_shared_rank_u32(smem_u32(&tail->full[st]), 0);
+                    if (leader) mbar_arrive_expect_tx(&tail->full[st], 2 * (kPABytes + kPBBytes));
+                    tma_load_2d_pair(sA + st * kPABytes, &tmX, full0, kb * kTileK, m0);
+                    tma_load_2d_pair(sB + st * kPBBytes, &tmW, full0, kb * kTileK, n0);
+                }
+            }
+            // The even CTA's full barriers count both CTAs' copies: before the pair leaves,
+            // the last stages' copies must have landed (on the normal path the MMAs already
+            // waited for them and these waits return at once).
+            if (leader)
+                for (int i = max(it - kPStages, 0); i < it; ++i)
+                    mbar_wait_drain(&tail->full[i % kPStages], (i / kPStages) & 1, p.status,
+                                    kTagPDrainLoad);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (leader) {
+            const uint32_t idesc = idesc_bf16_f32(2 * kTBM, kTBN, false);  // both K-major
+            const uint64_t dA0 = smem_desc_sw128(smem_u32(sA), 16, 1024);
+            const uint64_t dB0 = smem_desc_sw128(smem_u32(sB), 16, 1024);
+            bool ok = true;
+            int it = 0, lt = 0;
+            PairWalk tw;
+            for (tw.start(p); ok && tw.valid(p); tw.next(p), ++lt) {
+                const int buf = lt & 1;
+                // Free once all eight epilogue warps read the tile before last.
+                if (lt >= 2 &&
+                    !(ok = __all_sync(0xFFFFFFFFu,
+                                      mbar_wait_cl(&tail->acc_empty[buf], ((lt >> 1) - 1) & 1,
+                                                   abort_flag, p.status, kTagPAccEmpty))))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * kTBN;
+                for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+                    const int st = it % kPStages;
+                    if (!(ok = __all_sync(0xFFFFFFFFu,
+                                          mbar_wait(&tail->full[st], (it / kPStages) & 1,
+                                                    abort_flag, p.status, kTagPFull))))
+                        break;
+                    tc_fence_after();
+                    const uint64_t dA = dA0 + (uint64_t)(st * (kPABytes >> 4));
+                    const uint64_t dB = dB0 + (uint64_t)(st * (kPBBytes >> 4));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)  // 16 K-elements = 32 bytes per MMA
+                        mma_pair_ss_warp(acc, dA + kk * 2, dB + kk * 2, idesc, (kb | kk) ? 1u : 0u);
+                    const uint32_t e = smem_u32(&tail->empty[st]);
+                    mma_pair_commit_warp(map_shared_rank_u32(e, 0));
+                    mma_pair_commit_warp(map_shared_rank_u32(e, 1));
+                }
+                if (ok) {
+                    const uint32_t a = smem_u32(&tail->acc_full[buf]);
+                    mma_pair_commit_warp(map_shared_rank_u32(a, 0));
+                    mma_pair_commit_warp(map_shared_rank_u32(a, 1));
+                }
+            }
+            // Leave only once every MMA issued above has completed: the TMEM of both CTAs is
+            // released after the closing cluster barrier.
+            mma_pair_commit_warp(map_shared_rank_u32(smem_u32(&tail->drain), 0));
+            mbar_wait_drain(&tail->drain, 0, p.status, kTagPDrainMma);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // the CTA-tile row (TMEM lane) this thread owns
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        int lt = 0;
+        float rs = 1.f;
+        PairWalk tw;
+        for (tw.start(p); tw.valid(p); tw.next(p), ++lt) {
+            const int buf = lt & 1;
+            const int mrow0 = tw.mt * (2 * kTBM) + (int)rank * kTBM;  // this CTA's first row
+            const int m = mrow0 + r;
+            const int n0 = tw.nt * kTBN;
+            // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run (as in
+            // gemm_tile_kernel); a pair that keeps one row block computes them once.
+            if ((p.flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
+                const int mq = mrow0 + quarter * 32;
+                for (int r4 = 0; r4 < 32; r4 += 4) {
+                    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int mr = mq + r4 + u;
+                        if (mr >= p.M) continue;
+                        const uint4* row = reinterpret_cast<const uint4*>(p.x + (size_t)mr * p.K);
+                        for (int c = lane; c < p.K / 8; c += 32) {
+                            float f[8];
+                            bf16x8_to_f32(__ldg(row + c), f);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
+                    }
+                    if (lane < 4) {
+                        const float v = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
+                        tail->rs[quarter * 32 + r4 + lane] = rsqrtf(v / (float)p.K + kNormEps);
+                    }
+                }
+                __syncwarp();
+                rs = tail->rs[quarter * 32 + lane];
+                __syncwarp();
+            }
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_cl(&tail->acc_full[buf], (lt >> 1) & 1,
+                                                      abort_flag, p.status, kTagPAccFull)))
+                break;
+            tc_fence_after();
+            for (int c = 0; c < kTBN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32_sync(tmem + buf * kTBN + 32 * c + lane_base, v);
+                if (c == kTBN / 32 - 1) {
+                    // This warp has read every column of the buffer: one arrival on the even
+                    // CTA's barrier, which frees the buffer once all eight warps have arrived.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_cluster(map_shared_rank_u32(smem_u32(&tail->acc_empty[buf]), 0));
+                }
+                if (m >= p.M) continue;
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) {
+                    const int n = n0 + 32 * c + 8 * g8;
+                    if (n >= p.N) break;
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[8 * g8 + e]);
+                    if (p.flags & NC_GEMM_NORM_INPUT) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] *= rs;
+                    }
+                    if (p.flags & NC_GEMM_RESIDUAL) {
+                        float rr[8];
+                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n), rr);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] += rr[e];
+                    }
+                    if (p.flags & NC_GEMM_RELU2) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float y = fmaxf(f[e], 0.f);
+                            f[e] = y * y;
+                        }
+                    }
+                    if (p.flags & NC_GEMM_TANH_CAP) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = p.cap * tanhf(f[e] / p.cap);
+                    }
+                    const int seg = p.seg_cols;
+                    bf16* dst = p.out + (size_t)(n / seg) * ((size_t)p.M * seg) + (size_t)m * seg +
+                                (n % seg);
+                    *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(f);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    // Neither CTA releases its tensor memory or leaves while the pair may still signal it.
+    cluster_arrive();
+    cluster_wait();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, kTTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -808,12 +1100,18 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
         e = cudaFuncSetAttribute(gemm_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kTSmemBytes);
         if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_pair_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+        if (e == cudaSuccess)
             e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return internal_cuda_fail(e);
         attr_set[dev] = true;
     }
+    // More than one 128-row block: CTA pairs on 256 x 256 tiles.
+    const bool pair = M > kTBM;
+    const int bm = pair ? 2 * kTBM : kTBM;
     CUtensorMap mx, mw;
-    if (!map_2d(&mx, x, M, K, kTBM, dev) || !map_2d(&mw, w, N, K, kTBN, dev))
+    if (!map_2d(&mx, x, M, K, kTBM, dev) || !map_2d(&mw, w, N, K, pair ? kTBN / 2 : kTBN, dev))
         return NC_ERR_INVALID_ARG;
     TileParams p;
     p.out = static_cast<bf16*>(out);
@@ -823,20 +1121,37 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
     p.N = N;
     p.K = K;
     p.kb_total = (K + kTileK - 1) / kTileK;
-    p.m_tiles = (M + kTBM - 1) / kTBM;
+    p.m_tiles = (M + bm - 1) / bm;
     p.n_tiles = (N + kTBN - 1) / kTBN;
     p.tiles = p.m_tiles * p.n_tiles;
-    // With at most one row block per SM, each CTA keeps a row block (its RMSNorm scales are
-    // computed once) and the grid is a whole number of CTAs per row block.
-    p.n_per = p.m_tiles <= sms[dev] ? std::min(p.n_tiles, sms[dev] / p.m_tiles) : 0;
+    // With at most one row block per worker (a CTA, or a pair), each worker keeps a row block
+    // (its RMSNorm scales are computed once) and the workers are a whole number per row block.
+    const int workers = pair ? sms[dev] / 2 : sms[dev];
+    p.n_per = p.m_tiles <= workers ? std::min(p.n_tiles, workers / p.m_tiles) : 0;
     p.flags = flags;
     p.cap = cap;
     p.seg_cols = seg_cols;
     p.status = status;
-    const unsigned grid =
-        (unsigned)(p.n_per ? p.m_tiles * p.n_per : std::min(p.tiles, sms[dev]));
-    gemm_tile_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(mx, mw, p);
-    e = cudaGetLastError();
+    const unsigned used =
+        (unsigned)(p.n_per ? p.m_tiles * p.n_per : std::min(p.tiles, workers));
+    if (!pair) {
+        gemm_tile_kernel<<<used, kTThreads, kTSmemBytes, stream>>>(mx, mw, p);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * used);
+    cfg.blockDim = dim3(kTThreads);
+    cfg.dynamicSmemBytes = kPSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, mx, mw, p);
     return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }
 

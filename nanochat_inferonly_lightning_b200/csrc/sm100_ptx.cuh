@@ -412,4 +412,129 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool b_mn_ma
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------------------------------
+// CTA pairs (cta_group::2): two CTAs of a cluster, ranks 2i and 2i+1, share one MMA of
+// M = 256 rows.  Each CTA holds its 128 rows of A and half of B's N columns in its own shared
+// memory at the same offsets; the even CTA issues the MMA, and each CTA's tensor memory
+// receives its own 128 rows of D.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the variable at this CTA's shared address `a` in CTA `rank`.
+__device__ __forceinline__ uint32_t map_shared_rank_u32(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// mbar_wait with cluster-scope acquire, for barriers that the peer CTA (or an MMA issued by
+// it) arrives on.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity, bool sleep) {
+    uint32_t ok;
+    if (sleep)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                             int* status, int tag) {
+    if (mbar_try_wait_cl(bar, parity, false)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cl(bar, parity, true)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                atomicOr(status, kStatusTimeoutMbar | tag);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ bool mbar_wait_drain_cl(uint64_t* bar, uint32_t parity, int* status,
+                                                   int tag) {
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait_cl(bar, parity, true)) return true;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > kDrainLimitNs) {
+            atomicOr(status, kStatusTimeoutMbar | tag);
+            return false;
+        }
+    }
+}
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+// Pair-wide TMEM allocation: one warp in each CTA of the pair, same warp index and same
+// holder offset; both CTAs receive the same column address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_holder, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_holder)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+// Tile load into this CTA's shared memory whose completion is counted on the mbarrier at
+// shared::cluster address `bar_cluster` (the even CTA's barrier, from map_shared_rank_u32).
+// No multicast: each CTA loads only its own half.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap,
+                                                 uint32_t bar_cluster, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+// Pair MMA from a converged warp (one elected lane issues): D (+)= A * B^T, kind::f16.
+__device__ __forceinline__ void mma_pair_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at shared::cluster address `bar_cluster` (this CTA's or the
+// peer's) when every pair MMA issued so far by the electing lane has completed.
+__device__ __forceinline__ void mma_pair_commit_warp(uint32_t bar_cluster) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+            bar_cluster)
+        : "memory");
+}
+
 }  // namespace nc
