@@ -1096,6 +1096,18 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
     if (st) return st;
     static bool attr_set[kMaxDev] = {};
     static int sms[kMaxDev] = {};
+    static int pairs_max[kMaxDev] = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kTThreads);
+    cfg.dynamicSmemBytes = kPSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (!attr_set[dev]) {
         e = cudaFuncSetAttribute(gemm_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kTSmemBytes);
@@ -1104,6 +1116,13 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
         if (e == cudaSuccess)
             e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        // Pairs that can be resident at once: a pair needs two SMs of one GPC, so an odd SM
+        // count per GPC leaves SMs that no pair can use.  More pairs than this would make a
+        // second wave.
+        if (e == cudaSuccess) {
+            cfg.gridDim = dim3(2);
+            e = cudaOccupancyMaxActiveClusters(&pairs_max[dev], gemm_pair_kernel, &cfg);
+        }
         if (e != cudaSuccess) return internal_cuda_fail(e);
         attr_set[dev] = true;
     }
@@ -1126,7 +1145,7 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
     p.tiles = p.m_tiles * p.n_tiles;
     // With at most one row block per worker (a CTA, or a pair), each worker keeps a row block
     // (its RMSNorm scales are computed once) and the workers are a whole number per row block.
-    const int workers = pair ? sms[dev] / 2 : sms[dev];
+    const int workers = pair ? std::max(1, std::min(sms[dev] / 2, pairs_max[dev])) : sms[dev];
     p.n_per = p.m_tiles <= workers ? std::min(p.n_tiles, workers / p.m_tiles) : 0;
     p.flags = flags;
     p.cap = cap;
@@ -1139,18 +1158,7 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
         e = cudaGetLastError();
         return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
     }
-    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * used);
-    cfg.blockDim = dim3(kTThreads);
-    cfg.dynamicSmemBytes = kPSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, mx, mw, p);
     return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }
