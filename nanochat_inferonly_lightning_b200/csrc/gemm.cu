@@ -656,6 +656,9 @@ struct PairWalk {
 constexpr int kTagPEmpty = 0x61, kTagPFull = 0x62, kTagPAccFull = 0x63, kTagPAccEmpty = 0x64,
               kTagPDrainLoad = 0x65, kTagPDrainMma = 0x66;
 
+// KF >= 0: the fused steps fixed at compile time (the prompt pass's combinations); -1: read
+// from flags.
+template <int KF>
 __global__ void __launch_bounds__(kTThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const TileParams p) {
@@ -667,6 +670,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     PairTail* tail = reinterpret_cast<PairTail*>(sB + kPStages * kPBBytes);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int flags = KF >= 0 ? KF : p.flags;
     const uint32_t rank = cluster_ctarank() & 1u;  // cluster = one pair
     const bool leader = rank == 0;
 
@@ -792,7 +796,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const int n0 = tw.nt * kTBN;
             // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run (as in
             // gemm_tile_kernel); a pair that keeps one row block computes them once.
-            if ((p.flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
+            if ((flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
                 const int mq = mrow0 + quarter * 32;
                 for (int r4 = 0; r4 < 32; r4 += 4) {
                     float ss[4] = {0.f, 0.f, 0.f, 0.f};
@@ -845,24 +849,24 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     float f[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[8 * g8 + e]);
-                    if (p.flags & NC_GEMM_NORM_INPUT) {
+                    if (flags & NC_GEMM_NORM_INPUT) {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) f[e] *= rs;
                     }
-                    if (p.flags & NC_GEMM_RESIDUAL) {
+                    if (flags & NC_GEMM_RESIDUAL) {
                         float rr[8];
                         bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n), rr);
 #pragma unroll
                         for (int e = 0; e < 8; ++e) f[e] += rr[e];
                     }
-                    if (p.flags & NC_GEMM_RELU2) {
+                    if (flags & NC_GEMM_RELU2) {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
                             const float y = fmaxf(f[e], 0.f);
                             f[e] = y * y;
                         }
                     }
-                    if (p.flags & NC_GEMM_TANH_CAP) {
+                    if (flags & NC_GEMM_TANH_CAP) {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) f[e] = p.cap * tanhf(f[e] / p.cap);
                     }
@@ -1014,6 +1018,18 @@ bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
     return x < y + bn && y < x + an;
 }
 
+cudaError_t set_pair_smem() {
+    cudaError_t e = cudaSuccess;
+    const void* fns[4] = {(const void*)gemm_pair_kernel<-1>,
+                          (const void*)gemm_pair_kernel<NC_GEMM_NORM_INPUT>,
+                          (const void*)gemm_pair_kernel<NC_GEMM_RESIDUAL>,
+                          (const void*)gemm_pair_kernel<NC_GEMM_NORM_INPUT | NC_GEMM_RELU2>};
+    for (const void* f : fns)
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+    return e;
+}
+
 }  // namespace
 
 }  // namespace nc
@@ -1112,8 +1128,7 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
         e = cudaFuncSetAttribute(gemm_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kTSmemBytes);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_pair_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+            e = set_pair_smem();
         if (e == cudaSuccess)
             e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         // Pairs that can be resident at once: a pair needs two SMs of one GPC, so an odd SM
@@ -1121,7 +1136,7 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
         // second wave.
         if (e == cudaSuccess) {
             cfg.gridDim = dim3(2);
-            e = cudaOccupancyMaxActiveClusters(&pairs_max[dev], gemm_pair_kernel, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&pairs_max[dev], gemm_pair_kernel<-1>, &cfg);
         }
         if (e != cudaSuccess) return internal_cuda_fail(e);
         attr_set[dev] = true;
@@ -1159,7 +1174,20 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
         return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
     }
     cfg.gridDim = dim3(2 * used);
-    e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, mx, mw, p);
+    switch (flags) {
+        case NC_GEMM_NORM_INPUT:
+            e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<NC_GEMM_NORM_INPUT>, mx, mw, p);
+            break;
+        case NC_GEMM_RESIDUAL:
+            e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<NC_GEMM_RESIDUAL>, mx, mw, p);
+            break;
+        case NC_GEMM_NORM_INPUT | NC_GEMM_RELU2:
+            e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<NC_GEMM_NORM_INPUT | NC_GEMM_RELU2>, mx,
+                                   mw, p);
+            break;
+        default:
+            e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<-1>, mx, mw, p);
+    }
     return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
 }
 
