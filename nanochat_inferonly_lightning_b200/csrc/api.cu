@@ -87,17 +87,34 @@ int status_word(int** out) {
     return NC_OK;
 }
 
-// Keys per split-KV chunk: for larger batches, aim for about four CTAs per SM over the whole
-// batch.
+// Keys per split-KV chunk for the streaming layout.  The persistent grid (one CTA per SM)
+// takes its (split, sequence) items from a queue, so a call costs about items / SMs rounds
+// plus, on average, half a round of tail, each round one item of T keys: T keys of streaming
+// and a fixed part (the stage ring's ramp, the partial's write, the combine) worth about 40
+// keys.  The host knows only the longest length, so the item count assumes an average of half
+// of it and one partial split per two sequences.  T is the multiple of 16 from 64 (up to
+// 1024) with the lowest estimated cost, at most 32 splits per sequence (the last split of a
+// head combines all of them).  Measured on cfg3's lengths: 64 sequences 99 us at the chosen
+// 160 keys against 110 us at the former rule (four items per CTA), the two 32-sequence halves
+// 55.4 / 74.5 us at the chosen 128 against 58.3 / 77.0.
 int auto_split_len(int batch, int max_kv_len) {
     // Small calls use the per-head layout (decode.cu), which takes 64 keys per split.
     if (decode_use_head_layout(batch, max_kv_len, 0)) return kDecodeHeadSplit;
+    constexpr int kSms = 148;
+    constexpr int kItemCostKeys = 40;
     const long long est_keys = batch > 1 ? (long long)batch * max_kv_len / 2 : max_kv_len;
-    const long long target = 148LL * 4;
-    long long t = (est_keys + target - 1) / target;
-    // At most 32 splits per sequence: the last split of a head combines all of them, and
-    // beyond that the combine's round trips outweigh the extra parallelism.
-    t = std::max<long long>(t, (max_kv_len + 31) / 32);
+    int best_t = 0;
+    long long best_cost = 0;
+    for (int t = 64; t <= 1024; t += 16) {
+        if ((max_kv_len + t - 1) / t > 32) continue;
+        const long long items = (est_keys + t - 1) / t + (batch + 1) / 2;
+        const long long cost = (2 * items + kSms) * (t + kItemCostKeys);  // x 2 * kSms
+        if (best_t == 0 || cost < best_cost) {
+            best_t = t;
+            best_cost = cost;
+        }
+    }
+    long long t = best_t;
     // A small batch that is too long for the per-head layout: longer splits, fewer partials to
     // combine (measured: 8 sequences x 1024 keys, 23.7 us with 80-key splits, 26.8 with 32).
     if (batch <= kDecodeHeadMaxBatch) t = std::max<long long>(t, 80);
