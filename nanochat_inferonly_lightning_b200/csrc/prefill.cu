@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const float mu = (m_ref == kNegInf) ? 0.f : m_ref;
                     // P = exp2(s * scale * log2e - mu), packed to bf16 pairs.  The scaling and
-                    // the row sum run on packed f32x2 pairs; one pair in four takes the FMA-pipe
+                    // the row sum run on packed f32x2 pairs; one pair in eight takes the FMA-pipe
                     // polynomial (input clamped to 127 so that it stays monotone) instead of
                     // MUFU.  Masked scores are -inf and give exactly 0.
                     const uint64_t nmu2 = f2_pack(-mu, -mu);
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; ++i) {
                         float x0, x1, p0, p1;
                         f2_unpack(f2_fma(f2_pack(s_[2 * i], s_[2 * i + 1]), sl2x2, nmu2), x0, x1);
-                        if ((i & 3) == 3) {
+                        if ((i & 7) == 7) {
                             exp2_poly2(fminf(x0, 127.f), fminf(x1, 127.f), p0, p1);
                         } else {
                             p0 = fast_exp2(x0);
