@@ -428,7 +428,9 @@ def build_cfg1(impl, seed):
 
 
 def bench_decode(impl, dist, stepper, K, Wm, peaks, traffic, lens_all, name):
-    a, b = W.shard(len(lens_all), dist.rank, dist.world)
+    # Independent sequences, cut into contiguous shares of about equal KV bytes (each rank's
+    # decode time follows the bytes it streams, not its sequence count).
+    a, b = W.shard_weighted(lens_all, dist.rank, dist.world)
     lens = lens_all[a:b]
     bytes_rank = W.decode_bytes(lens) if lens else 0
     t_ms = 0.0

@@ -149,3 +149,30 @@ def shard(n_items, rank, world):
     base, rem = divmod(n_items, world)
     start = rank * base + min(rank, rem)
     return start, start + base + (1 if rank < rem else 0)
+
+
+def shard_weighted(weights, rank, world):
+    """Contiguous share [start, stop) of the items for `rank` of `world`, with the cut points
+    placed so that each rank's sum of weights (a sequence's KV length: the bytes its decode
+    streams) is as close as possible to an equal share: cut r goes at the first prefix whose
+    sum reaches r/world of the total, or just before it when that is strictly closer.  Every rank gets at
+    least one item when there are at least `world` items."""
+    n = len(weights)
+    if world <= 1 or n == 0:
+        return (0, n) if rank == 0 or world <= 1 else (n, n)
+    total = float(sum(weights))
+    prefix = [0.0]
+    for w in weights:
+        prefix.append(prefix[-1] + float(w))
+    cuts = [0]
+    for r in range(1, world):
+        target = total * r / world
+        i = next((k for k in range(1, n + 1) if prefix[k] >= target), n)
+        if i > 0 and abs(prefix[i - 1] - target) < abs(prefix[i] - target):
+            i -= 1
+        lo = cuts[-1] + (1 if n >= world else 0)   # at least one item per earlier rank
+        hi = n - (world - r if n >= world else 0)  # and one left for every later rank
+        cuts.append(min(max(i, lo), hi))
+    cuts.append(n)
+    return cuts[rank], cuts[rank + 1]
+

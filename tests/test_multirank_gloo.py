@@ -55,6 +55,26 @@ def test_shards_cover_every_sequence_once():
             assert max(sizes) - min(sizes) <= 1
 
 
+def test_weighted_shards_cover_every_sequence_once_and_balance_bytes():
+    """The decode benches cut the sequences into contiguous shares of about equal KV length:
+    every sequence once, in order, at least one per rank when there are enough, and each
+    rank's sum within one sequence's length of an equal share."""
+    from nanochat_inferonly_lightning_b200 import workloads as W
+
+    cases = [W.cfg3_kv_lens(), [512], [5, 1, 1, 1], [7] * 9, list(range(1, 40))]
+    for lens in cases:
+        for world in (1, 2, 4, 8):
+            spans = [W.shard_weighted(lens, r, world) for r in range(world)]
+            covered = [i for a, b in spans for i in range(a, b)]
+            assert covered == list(range(len(lens)))
+            if len(lens) >= world:
+                assert all(b > a for a, b in spans)
+                share = sum(lens) / world
+                assert all(abs(sum(lens[a:b]) - share) <= max(lens) * (1 + 1e-9)
+                           for a, b in spans), (lens, world, spans)
+    assert W.shard_weighted([512], 0, 2) == (0, 1)
+
+
 def test_two_ranks_shard_and_reduce():
     outs = run_ranks("""
         d = bench.Dist(2, backend="gloo", timeout_s=30)
