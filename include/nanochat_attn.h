@@ -289,7 +289,10 @@ int nc_gemm_skinny(void* out, const void* x, const void* w, const void* residual
  * tcgen05 kernel with 128 x 256 output tiles, both operands staged by TMA, fp32 accumulation
  * in tensor memory, one bf16 rounding.  Same flags, order and seg_cols as nc_gemm_skinny.
  * Requirements: N % 8 == 0, K % 8 == 0, seg_cols % 8 == 0; x, w, out and residual 16-byte
- * aligned; out must not overlap x (residual may equal out).  Deterministic.
+ * aligned; out must not overlap x (residual may equal out).  Deterministic.  M > 128 runs on
+ * CTA pairs (256 x 256 tiles).  Launched as a programmatic dependent of the previous kernel
+ * in the stream: its setup may overlap that kernel's tail, and it reads nothing before that
+ * kernel has completed.
  * Replaces: gemm_half / gemm_half_residual for M > 16 (kernels/gemm.cu:14-51, the 128 x 128
  * CUTLASS tiles) at the prompt call sites src/model.cpp:114-116, :139, :149-150, :153, together
  * with the rmsnorm / relu_squared launches around them. */

@@ -424,6 +424,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tail->tmem;
     volatile int* abort_flag = &tail->abort;
+    // Programmatic dependent launch: the setup above may overlap the previous kernel's tail;
+    // nothing in global memory is read or written before this wait, which returns once that
+    // kernel has completed and its writes are visible.
+    griddep_launch_dependents();
+    griddep_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -703,6 +708,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tail->tmem;
     volatile int* abort_flag = &tail->abort;
+    // Programmatic dependent launch, as in gemm_tile_kernel.
+    griddep_launch_dependents();
+    griddep_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -1113,7 +1121,7 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
     static bool attr_set[kMaxDev] = {};
     static int sms[kMaxDev] = {};
     static int pairs_max[kMaxDev] = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
@@ -1168,11 +1176,21 @@ int nc_gemm(void* out, const void* x, const void* w, const void* residual, int M
     p.status = status;
     const unsigned used =
         (unsigned)(p.n_per ? p.m_tiles * p.n_per : std::min(p.tiles, workers));
+    // Both kernels are launched as programmatic dependents of the previous kernel in the stream.
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     if (!pair) {
-        gemm_tile_kernel<<<used, kTThreads, kTSmemBytes, stream>>>(mx, mw, p);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t tcfg = {};
+        tcfg.gridDim = dim3(used);
+        tcfg.blockDim = dim3(kTThreads);
+        tcfg.dynamicSmemBytes = kTSmemBytes;
+        tcfg.stream = stream;
+        tcfg.attrs = &attr[1];
+        tcfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&tcfg, gemm_tile_kernel, mx, mw, p);
         return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
     }
+    cfg.numAttrs = 2;
     cfg.gridDim = dim3(2 * used);
     switch (flags) {
         case NC_GEMM_NORM_INPUT:
