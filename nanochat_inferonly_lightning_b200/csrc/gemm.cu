@@ -308,8 +308,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 }
 
 // ---------------------------------------------------------------------------------------
-// Prompt-pass GEMM (any M, sized for M in the hundreds to thousands): persistent, one CTA per
-// SM, 128 x 256 output tiles (one tcgen05.mma of M = 128 rows of x, N = 256 output features,
+// Prompt-pass GEMM on single CTAs (nc_gemm for M <= 128; larger M runs on the CTA pairs of
+// gemm_pair_kernel below, which keeps these roles): persistent, one CTA per SM, 128 x 256
+// output tiles (one tcgen05.mma of M = 128 rows of x, N = 256 output features,
 // K = 16 per step), x and w boxes staged by TMA (no multicast) through a 4-stage ring of
 // 48 KB stages, and two 256-column accumulators in TMEM so that the epilogue of one tile
 // overlaps the MMAs of the next.  Tiles are numbered with the row block fastest, so the CTAs
