@@ -241,12 +241,13 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
 // Small decode calls run the per-head layout: one CTA per (split, head, sequence) with at
 // most kDecodeHeadSplit keys per split.  It is chosen for at most kDecodeHeadMaxBatch sequences
 // and, with automatic splits, at most kDecodeHeadMaxKeys keys in total (batch * max_kv_len).
-// Measured at 8 sequences: 14.4 us against 20.8 for the streaming layout at 512 keys, level
-// (23.1 against 23.3) at 1024 keys, so the bound is 8 x 1024.  An explicit split length above
-// kDecodeHeadSplit selects the streaming layout.
+// With the cache rows staged in shared memory (six CTAs per SM), measured at 8 sequences of
+// cfg3's lengths (longest ~2048): 22.1 / 18.5 / 26.7 us against 24.7 / 22.3 / 29.1 for the
+// streaming layout, and at 8 x 4096 keys 65.3 against 59.6, so the bound is 8 x 2048.  An
+// explicit split length above kDecodeHeadSplit selects the streaming layout.
 constexpr int kDecodeHeadMaxBatch = 8;
 constexpr int kDecodeHeadSplit = 64;
-constexpr long long kDecodeHeadMaxKeys = 8192;
+constexpr long long kDecodeHeadMaxKeys = 16384;
 inline bool decode_use_head_layout(int batch, int max_kv_len, int split_len) {
     if (batch > kDecodeHeadMaxBatch) return false;
     if (split_len) return split_len <= kDecodeHeadSplit;
