@@ -545,7 +545,24 @@ __global__ void __launch_bounds__(kTThreads, 1)
                                                    p.status, kTagTAccFull)))
                 break;
             tc_fence_after();
+            // The residual of the first chunk, then each next chunk's ahead of this one's work:
+            // its loads are in flight while this chunk is read from TMEM and stored.
+            uint4 rnext[4];
+            auto load_res = [&](int c, uint4 (&r)[4]) {
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) {
+                    const int n = n0 + 32 * c + 8 * g8;
+                    r[g8] = ((p.flags & NC_GEMM_RESIDUAL) && m < p.M && n < p.N)
+                                ? *reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n)
+                                : make_uint4(0u, 0u, 0u, 0u);
+                }
+            };
+            load_res(0, rnext);
             for (int c = 0; c < kTBN / 32; ++c) {
+                uint4 rcur[4];
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) rcur[g8] = rnext[g8];
+                if (c + 1 < kTBN / 32) load_res(c + 1, rnext);
                 uint32_t v[32];
                 tmem_ld32_sync(tmem + buf * kTBN + 32 * c + lane_base, v);
                 if (c == kTBN / 32 - 1) {
@@ -568,7 +585,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                     if (p.flags & NC_GEMM_RESIDUAL) {
                         float rr[8];
-                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n), rr);
+                        bf16x8_to_f32(rcur[g8], rr);
 #pragma unroll
                         for (int e = 0; e < 8; ++e) f[e] += rr[e];
                     }
@@ -839,7 +856,24 @@ __global__ void __launch_bounds__(kTThreads, 1)
                                                       abort_flag, p.status, kTagPAccFull)))
                 break;
             tc_fence_after();
+            // The residual of the first chunk, then each next chunk's ahead of this one's work:
+            // its loads are in flight while this chunk is read from TMEM and stored.
+            uint4 rnext[4];
+            auto load_res = [&](int c, uint4 (&r)[4]) {
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) {
+                    const int n = n0 + 32 * c + 8 * g8;
+                    r[g8] = ((flags & NC_GEMM_RESIDUAL) && m < p.M && n < p.N)
+                                ? *reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n)
+                                : make_uint4(0u, 0u, 0u, 0u);
+                }
+            };
+            load_res(0, rnext);
             for (int c = 0; c < kTBN / 32; ++c) {
+                uint4 rcur[4];
+#pragma unroll
+                for (int g8 = 0; g8 < 4; ++g8) rcur[g8] = rnext[g8];
+                if (c + 1 < kTBN / 32) load_res(c + 1, rnext);
                 uint32_t v[32];
                 tmem_ld32_sync(tmem + buf * kTBN + 32 * c + lane_base, v);
                 if (c == kTBN / 32 - 1) {
@@ -864,7 +898,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                     if (flags & NC_GEMM_RESIDUAL) {
                         float rr[8];
-                        bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.N + n), rr);
+                        bf16x8_to_f32(rcur[g8], rr);
 #pragma unroll
                         for (int e = 0; e < 8; ++e) f[e] += rr[e];
                     }
