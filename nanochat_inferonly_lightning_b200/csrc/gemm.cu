@@ -384,6 +384,52 @@ struct TileWalk {
     }
 };
 
+// RMSNorm scales of 32 rows [mq, mq + 32) of x (reference kernels/rmsnorm.cu:17-48: fp32 sum of
+// squares, rsqrt(sum / K + 1e-6)) by one warp, into rs_out[0..32): four rows at a time, each
+// lane summing the 16-byte pieces lane, lane + 32, ... of a row in order, then a butterfly sum.
+// The pieces of the four rows (up to nine per lane and row, K <= 2304 in one round) are all
+// loaded before any is summed, so a group of rows costs one memory round trip.
+__device__ __forceinline__ void row_scales_warp(const bf16* x, int M, int K, int mq, int lane,
+                                                float* rs_out) {
+    constexpr int kPieces = 9;
+    const int kp = K / 8;  // 16-byte pieces per row
+    for (int r4 = 0; r4 < 32; r4 += 4) {
+        float ss[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = lane; c0 < kp; c0 += 32 * kPieces) {
+            uint4 v[4][kPieces];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int mr = mq + r4 + u;
+                const uint4* row = reinterpret_cast<const uint4*>(x + (size_t)(mr < M ? mr : 0) * K);
+#pragma unroll
+                for (int j = 0; j < kPieces; ++j) {
+                    const int c = c0 + 32 * j;
+                    v[u][j] = (mr < M && c < kp) ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                for (int j = 0; j < kPieces; ++j) {
+                    float f[8];
+                    bf16x8_to_f32(v[u][j], f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
+        }
+        if (lane < 4) {
+            const float t = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
+            rs_out[r4 + lane] = rsqrtf(t / (float)K + kNormEps);
+        }
+    }
+}
+
 constexpr int kTagTEmpty = 0x51, kTagTFull = 0x52, kTagTAccFull = 0x53, kTagTAccEmpty = 0x54,
               kTagTDrainLoad = 0x55, kTagTDrainMma = 0x56;
 
@@ -507,36 +553,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const int buf = lt & 1;
             const int m = tw.mt * kTBM + r;
             const int n0 = tw.nt * kTBN;
-            // RMSNorm scale of the warp's 32 rows (reference kernels/rmsnorm.cu:17-48: fp32
-            // sum of squares, rsqrt(sum / K + 1e-6)), while the tile's MMAs run: four rows at a
-            // time, the 32 lanes reading consecutive 16-byte pieces of each (coalesced), then a
-            // butterfly sum.  A CTA that keeps one row block computes them once.
+            // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run.  A CTA that keeps
+            // one row block computes them once.
             if ((p.flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
-                const int mq = tw.mt * kTBM + quarter * 32;
-                for (int r4 = 0; r4 < 32; r4 += 4) {
-                    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int mr = mq + r4 + u;
-                        if (mr >= p.M) continue;
-                        const uint4* row = reinterpret_cast<const uint4*>(p.x + (size_t)mr * p.K);
-                        for (int c = lane; c < p.K / 8; c += 32) {
-                            float f[8];
-                            bf16x8_to_f32(__ldg(row + c), f);
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
-                    }
-                    if (lane < 4) {
-                        const float v = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
-                        tail->rs[quarter * 32 + r4 + lane] = rsqrtf(v / (float)p.K + kNormEps);
-                    }
-                }
+                row_scales_warp(p.x, p.M, p.K, tw.mt * kTBM + quarter * 32, lane,
+                                tail->rs + quarter * 32);
                 __syncwarp();
                 rs = tail->rs[quarter * 32 + lane];
                 __syncwarp();  // read before the next tile's scales overwrite it
@@ -820,34 +841,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const int mrow0 = tw.mt * (2 * kTBM) + (int)rank * kTBM;  // this CTA's first row
             const int m = mrow0 + r;
             const int n0 = tw.nt * kTBN;
-            // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run (as in
-            // gemm_tile_kernel); a pair that keeps one row block computes them once.
+            // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run; a pair that keeps
+            // one row block computes them once.
             if ((flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
-                const int mq = mrow0 + quarter * 32;
-                for (int r4 = 0; r4 < 32; r4 += 4) {
-                    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int mr = mq + r4 + u;
-                        if (mr >= p.M) continue;
-                        const uint4* row = reinterpret_cast<const uint4*>(p.x + (size_t)mr * p.K);
-                        for (int c = lane; c < p.K / 8; c += 32) {
-                            float f[8];
-                            bf16x8_to_f32(__ldg(row + c), f);
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
-                    }
-                    if (lane < 4) {
-                        const float v = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
-                        tail->rs[quarter * 32 + r4 + lane] = rsqrtf(v / (float)p.K + kNormEps);
-                    }
-                }
+                row_scales_warp(p.x, p.M, p.K, mrow0 + quarter * 32, lane, tail->rs + quarter * 32);
                 __syncwarp();
                 rs = tail->rs[quarter * 32 + lane];
                 __syncwarp();
