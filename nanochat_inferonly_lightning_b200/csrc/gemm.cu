@@ -64,6 +64,54 @@ struct GemmTail {
     int abort;
 };
 
+// RMSNorm scales (reference kernels/rmsnorm.cu:17-48: fp32 sum of squares, rsqrt(sum / K +
+// 1e-6)) of `count` rows of x, row i = mq + i * step, into rs_out[i * step], by one warp: four
+// rows at a time, each lane summing the 16-byte pieces lane, lane + 32, ... of a row in order,
+// then a butterfly sum.  The pieces of the four rows (up to nine per lane and row, K <= 2304 in
+// one round) are all loaded before any is summed, so a group of rows costs one memory round
+// trip.  Rows at or past M get the scale of an all-zero row.  Plain (coherent) loads: x may
+// have been written by the kernel this one overlaps through programmatic dependent launch.
+__device__ __forceinline__ void row_scales_warp(const bf16* x, int M, int K, int mq, int step,
+                                                int count, int lane, float* rs_out) {
+    constexpr int kPieces = 9;
+    const int kp = K / 8;  // 16-byte pieces per row
+    for (int r4 = 0; r4 < count; r4 += 4) {
+        float ss[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = lane; c0 < kp; c0 += 32 * kPieces) {
+            uint4 v[4][kPieces];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int mr = mq + (r4 + u) * step;
+                const uint4* row = reinterpret_cast<const uint4*>(x + (size_t)(mr < M ? mr : 0) * K);
+#pragma unroll
+                for (int j = 0; j < kPieces; ++j) {
+                    const int c = c0 + 32 * j;
+                    v[u][j] = (mr < M && c < kp) ? row[c] : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+#pragma unroll
+                for (int j = 0; j < kPieces; ++j) {
+                    float f[8];
+                    bf16x8_to_f32(v[u][j], f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
+        }
+        if (lane < 4 && r4 + lane < count) {
+            const float t = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
+            rs_out[(r4 + lane) * step] = rsqrtf(t / (float)K + kNormEps);
+        }
+    }
+}
+
 template <int MP>
 constexpr int gemm_smem_bytes() {
     return kStages * (kWBoxBytes + MP * 128) + (int)sizeof(GemmTail) + 1024;
@@ -219,21 +267,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         const int n = n0 + quarter * 32 + lane;
         griddep_wait();
         if (p.flags & NC_GEMM_NORM_INPUT) {
-            // RMSNorm scale of each input row (reference kernels/rmsnorm.cu:17-48:
-            // rsqrt(sum(x^2) / n + 1e-6), fp32).
-            for (int m = warp - 2; m < p.M; m += 4) {
-                const bf16* row = p.x + (size_t)m * p.K;
-                float ss = 0.f;
-                for (int c = lane * 8; c < p.K; c += 256) {
-                    float f[8];
-                    bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) ss = __fmaf_rn(f[e], f[e], ss);
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-                if (lane == 0) tail->rnorm[m] = rsqrtf(ss / (float)p.K + kNormEps);
-            }
+            // RMSNorm scale of each input row, rows m = warp - 2 (mod 4) in this warp.
+            const int m0 = warp - 2;
+            if (m0 < p.M)
+                row_scales_warp(p.x, p.M, p.K, m0, 4, (p.M - m0 + 3) / 4, lane, tail->rnorm + m0);
         }
         float acc[MP];
 #pragma unroll
@@ -384,52 +421,6 @@ struct TileWalk {
     }
 };
 
-// RMSNorm scales of 32 rows [mq, mq + 32) of x (reference kernels/rmsnorm.cu:17-48: fp32 sum of
-// squares, rsqrt(sum / K + 1e-6)) by one warp, into rs_out[0..32): four rows at a time, each
-// lane summing the 16-byte pieces lane, lane + 32, ... of a row in order, then a butterfly sum.
-// The pieces of the four rows (up to nine per lane and row, K <= 2304 in one round) are all
-// loaded before any is summed, so a group of rows costs one memory round trip.
-__device__ __forceinline__ void row_scales_warp(const bf16* x, int M, int K, int mq, int lane,
-                                                float* rs_out) {
-    constexpr int kPieces = 9;
-    const int kp = K / 8;  // 16-byte pieces per row
-    for (int r4 = 0; r4 < 32; r4 += 4) {
-        float ss[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c0 = lane; c0 < kp; c0 += 32 * kPieces) {
-            uint4 v[4][kPieces];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int mr = mq + r4 + u;
-                const uint4* row = reinterpret_cast<const uint4*>(x + (size_t)(mr < M ? mr : 0) * K);
-#pragma unroll
-                for (int j = 0; j < kPieces; ++j) {
-                    const int c = c0 + 32 * j;
-                    v[u][j] = (mr < M && c < kp) ? __ldg(row + c) : make_uint4(0u, 0u, 0u, 0u);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                for (int j = 0; j < kPieces; ++j) {
-                    float f[8];
-                    bf16x8_to_f32(v[u][j], f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) ss[u] = __fmaf_rn(f[e], f[e], ss[u]);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss[u] += __shfl_xor_sync(0xFFFFFFFFu, ss[u], o);
-        }
-        if (lane < 4) {
-            const float t = lane == 0 ? ss[0] : lane == 1 ? ss[1] : lane == 2 ? ss[2] : ss[3];
-            rs_out[r4 + lane] = rsqrtf(t / (float)K + kNormEps);
-        }
-    }
-}
-
 constexpr int kTagTEmpty = 0x51, kTagTFull = 0x52, kTagTAccFull = 0x53, kTagTAccEmpty = 0x54,
               kTagTDrainLoad = 0x55, kTagTDrainMma = 0x56;
 
@@ -556,7 +547,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run.  A CTA that keeps
             // one row block computes them once.
             if ((p.flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
-                row_scales_warp(p.x, p.M, p.K, tw.mt * kTBM + quarter * 32, lane,
+                row_scales_warp(p.x, p.M, p.K, tw.mt * kTBM + quarter * 32, 1, 32, lane,
                                 tail->rs + quarter * 32);
                 __syncwarp();
                 rs = tail->rs[quarter * 32 + lane];
@@ -844,7 +835,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
             // RMSNorm scale of the warp's 32 rows, while the tile's MMAs run; a pair that keeps
             // one row block computes them once.
             if ((flags & NC_GEMM_NORM_INPUT) && (lt == 0 || !p.n_per)) {
-                row_scales_warp(p.x, p.M, p.K, mrow0 + quarter * 32, lane, tail->rs + quarter * 32);
+                row_scales_warp(p.x, p.M, p.K, mrow0 + quarter * 32, 1, 32, lane,
+                                tail->rs + quarter * 32);
                 __syncwarp();
                 rs = tail->rs[quarter * 32 + lane];
                 __syncwarp();
