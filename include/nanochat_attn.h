@@ -317,13 +317,15 @@ int nc_argmax_rows(int* out, const void* logits, int rows, int cols, cudaStream_
 /* out[r] = a token drawn from row r of the logits (bf16 [rows, vocab], vocab % 8 == 0) as
  * Engine::sample does it (src/engine.cpp:62-131): temperature == 0 is greedy (nc_argmax_rows);
  * otherwise softmax of (l - max) / temperature over the whole row, the top_k largest
- * (top_k <= 1024; top_k <= 0 or >= vocab: no top-k filter, which requires top_p >= 1 and then
- * samples the whole row in index order), then top_p (>= 1: off) on them in descending order, a
- * renormalisation, and the first entry whose running sum exceeds uniforms[r] (a device array
- * [rows] of draws in [0, 1), which the caller generates; the reference draws them from its
- * mt19937).  Equal probabilities are taken in ascending index order (the reference's sort
- * leaves their order unspecified).  The top-p cut, the renormalisation and the running sums are
- * the reference's sequential fp32 sums; the softmax denominator is a parallel fp32 sum. */
+ * (top_k <= 1024; top_k <= 0 or >= vocab: no top-k filter), then top_p (>= 1: off) on them in
+ * descending order, a renormalisation, and the first entry whose running sum exceeds
+ * uniforms[r] (a device array [rows] of draws in [0, 1), which the caller generates; the
+ * reference draws them from its mt19937).  With neither filter the row is sampled in index
+ * order.  Equal probabilities are taken in ascending index order (the reference's sort leaves
+ * their order unspecified).  With top-k, the top-p cut, the renormalisation and the running
+ * sums are the reference's sequential fp32 sums; top-p over the whole row (top_k off) finds the
+ * cut and the draw from exact sums of the probabilities, without a sort; the softmax
+ * denominator is a parallel fp32 sum. */
 int nc_sample_rows(int* out, const void* logits, int rows, int vocab, float temperature,
                    int top_k, float top_p, const float* uniforms, cudaStream_t stream);
 

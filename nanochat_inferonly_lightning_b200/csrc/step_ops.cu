@@ -208,6 +208,247 @@ struct SampleSmem {
     int found;
 };
 
+// ---------------------------------------------------------------------------------------
+// Top-p over the whole row (Engine::top_p_filter with top_k off, src/engine.cpp:68-84, then
+// the renormalisation and the draw, :114-131), without a sort.  A probability is a monotone
+// function of its bf16 logit, so the reference's descending sort orders the row by 16-bit key
+// (equal keys by ascending index: the order its sort leaves unspecified; -0 counts as +0), and
+// all members of one key have the same probability.  One pass counts the members of every key
+// (65536 16-bit counters, 128 KB of shared memory); the mass of a key is then its count times
+// its probability, in fixed point (units of 2^-62, a probability being at most 1), so every
+// sum below is exact and independent of the order of the threads.  The keys' masses summed
+// over 256 buckets of 256 keys locate the bucket where the running mass (from the top) first
+// exceeds top_p, the masses of that bucket's keys locate the key, and the members of that key
+// needed to pass top_p are counted off; the draw r is located in the kept prefix the same way,
+// and a last pass over the row finds the chosen member's index.  The reference sums in fp32,
+// in order: the two agree except where top_p or r lies within that summation error of an
+// interval edge.
+// ---------------------------------------------------------------------------------------
+constexpr size_t kTopPCountBytes = 65536 * sizeof(uint16_t);
+constexpr int kTopPMaxDev = 64;  // devices whose shared-memory attribute is tracked
+
+struct TopPSmem {
+    int warp_sums[32];
+    float fred[32];
+    int cnt1[256], cnt2[256];  // per bucket: members of the 256 keys of a high byte / of one key
+    unsigned long long mass1[256], mass2[256];
+    int xb;
+    unsigned long long xmass;
+    int found, all_equal;
+};
+
+// Fixed-point mass of one member of key `key` (units of 2^-62).
+__device__ __forceinline__ unsigned long long key_mass(uint32_t key, float mx, float temperature,
+                                                       float sum) {
+    const float q = expf((key_value(key) - mx) / temperature) / sum;
+    return (unsigned long long)(q * 0x1p62f);
+}
+
+// Warp 0: walking the 256 buckets of (cnt, mass) from 255 down, the first bucket at which the
+// running mass exceeds `target`; sm.xb = that bucket (-1 if the total does not), sm.xmass = the
+// mass of the buckets above it (the total when there is none).  Lane l scans buckets 255 - 8l
+// down to 248 - 8l.
+__device__ void bucket_crossing(TopPSmem& sm, const int* cnt, const unsigned long long* mass,
+                                unsigned long long target) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long m = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m += mass[255 - 8 * lane - i];
+    unsigned long long mi = m;  // inclusive scan over the lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+        if (lane >= o) mi += y;
+    }
+    const unsigned long long total = __shfl_sync(0xFFFFFFFFu, mi, 31);
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, mi > target);
+    if (hit == 0u) {
+        if (lane == 0) {
+            sm.xb = -1;
+            sm.xmass = total;
+        }
+        return;
+    }
+    if (lane == __ffs(hit) - 1) {
+        unsigned long long cum = mi - m;
+        int b = 255 - 8 * lane;
+        for (int i = 0; i < 7; ++i, --b) {  // the crossing lies in this lane's eight buckets
+            if (cum + mass[b] > target) break;
+            cum += mass[b];
+        }
+        sm.xb = b;
+        sm.xmass = cum;
+    }
+    (void)cnt;
+}
+
+// Every thread: the crossing of `target` in (cnt, mass), searched by warp 0.
+__device__ void block_crossing(TopPSmem& sm, const int* cnt, const unsigned long long* mass,
+                               unsigned long long target, int* b, unsigned long long* above) {
+    __syncthreads();  // (cnt, mass) written; earlier readers of sm.xb done
+    if (threadIdx.x < 32) bucket_crossing(sm, cnt, mass, target);
+    __syncthreads();
+    *b = sm.xb;
+    *above = sm.xmass;
+}
+
+__global__ void __launch_bounds__(kSampleThreads)
+    sample_top_p_kernel(int* __restrict__ out, const bf16* __restrict__ logits, int vocab,
+                        float temperature, float top_p, const float* __restrict__ uniforms) {
+    extern __shared__ __align__(16) uint32_t kcnt[];  // 65536 16-bit counters, two per word
+    __shared__ TopPSmem sm;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bf16* row = logits + (size_t)blockIdx.x * vocab;
+    const int ept = (((vocab + kSampleThreads - 1) / kSampleThreads) + 7) & ~7;
+    const int c0 = min(tid * ept, vocab), c1 = min(c0 + ept, vocab);
+    for (int i = tid; i < 32768; i += kSampleThreads) kcnt[i] = 0u;
+    // maximum logit and the softmax denominator, as sample_rows_kernel computes them
+    float mx = -INFINITY;
+    for (int c = c0; c < c1; c += 8) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, f[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) sm.fred[warp] = mx;
+    __syncthreads();
+    mx = sm.fred[0];
+    for (int w = 1; w < 32; ++w) mx = fmaxf(mx, sm.fred[w]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int c = c0; c < c1; c += 8) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += expf((f[e] - mx) / temperature);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if (lane == 0) sm.fred[warp] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int w = 0; w < 32; ++w) sum += sm.fred[w];
+    // members per key.  A 16-bit counter overflows only when all 65536 entries share one key:
+    // that row is flagged and handled with its single key below.
+    const uint32_t key0 = order_key(__bfloat16_as_ushort(row[0]));
+    bool same = true;
+    for (int c = c0; c < c1; c += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t key = order_key((w4[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            same &= key == key0;
+            atomicAdd(&kcnt[key >> 1], 1u << (16 * (key & 1)));
+        }
+    }
+    const bool all_equal = __syncthreads_and(same) != 0;
+    auto count_of = [&](uint32_t key) -> int {
+        if (all_equal) return key == key0 ? vocab : 0;
+        return (int)((kcnt[key >> 1] >> (16 * (key & 1))) & 0xFFFFu);
+    };
+    // level 1: thread t sums keys [64t, 64t + 64); four threads make one bucket (high byte)
+    {
+        int n = 0;
+        unsigned long long m = 0;
+        for (int i = 0; i < 64; ++i) {
+            const uint32_t key = (uint32_t)(64 * tid + i);
+            const int cn = count_of(key);
+            if (cn) {
+                n += cn;
+                m += (unsigned long long)cn * key_mass(key, mx, temperature, sum);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            n += __shfl_xor_sync(0xFFFFFFFFu, n, o);
+            m += __shfl_xor_sync(0xFFFFFFFFu, m, o);
+        }
+        if ((tid & 3) == 0) {
+            sm.cnt1[tid >> 2] = n;
+            sm.mass1[tid >> 2] = m;
+        }
+    }
+    // level 2 of high byte hb: one key per bucket (threads 0..255)
+    auto fill_level2 = [&](int hb) {
+        __syncthreads();  // earlier readers of cnt2 / mass2 done
+        if (tid < 256) {
+            const uint32_t key = ((uint32_t)hb << 8) | (uint32_t)tid;
+            const int cn = count_of(key);
+            sm.cnt2[tid] = cn;
+            sm.mass2[tid] = cn ? (unsigned long long)cn * key_mass(key, mx, temperature, sum) : 0ull;
+        }
+    };
+    const unsigned long long P = (unsigned long long)((double)top_p * 0x1p62);
+    int b1;
+    unsigned long long above1;
+    block_crossing(sm, sm.cnt1, sm.mass1, P, &b1, &above1);
+    unsigned long long S2 = above1;  // mass of the kept prefix (no cut: the total)
+    int kc = -1;                     // key of the group the cut falls in (-1: no cut)
+    int jc = 0;                      // members of key kc kept
+    if (b1 >= 0) {
+        fill_level2(b1);
+        int b2;
+        unsigned long long above2;
+        block_crossing(sm, sm.cnt2, sm.mass2, P - above1, &b2, &above2);
+        if (b2 >= 0) {  // always: bucket b1's mass carries the running sum past P
+            kc = (b1 << 8) | b2;
+            const unsigned long long above_c = above1 + above2;
+            const int gc = sm.cnt2[b2];
+            const unsigned long long qc = sm.mass2[b2] / (unsigned long long)gc;
+            jc = (int)((P - above_c) / qc) + 1;  // the first member whose running sum exceeds P
+            if (jc > gc) jc = gc;
+            S2 = above_c + (unsigned long long)jc * qc;
+        }
+    }
+    // The draw: the first entry of the prefix whose running sum exceeds r * S2 (the reference
+    // compares r with running sums of p / S2); r < 1 keeps the target inside the prefix.
+    unsigned long long T = (unsigned long long)((double)uniforms[blockIdx.x] * (double)S2);
+    if (T >= S2) T = S2 > 0 ? S2 - 1 : 0;
+    int br;
+    unsigned long long above_r1;
+    block_crossing(sm, sm.cnt1, sm.mass1, T, &br, &above_r1);
+    int kr = kc, jr = jc - 1;  // fallback (not reached): the prefix's last member
+    if (br >= 0) {
+        if (br != b1) fill_level2(br);
+        int b2;
+        unsigned long long above2;
+        block_crossing(sm, sm.cnt2, sm.mass2, T - above_r1, &b2, &above2);
+        if (b2 >= 0) {
+            kr = (br << 8) | b2;
+            const int g = sm.cnt2[b2];
+            const unsigned long long q = sm.mass2[b2] / (unsigned long long)g;
+            jr = (int)((T - above_r1 - above2) / q);
+            const int lim = kr == kc ? jc : g;
+            if (jr > lim - 1) jr = lim - 1;
+        }
+    }
+    // index of member jr (in ascending index order) of key kr
+    int n = 0;
+    if (kr >= 0)
+        for (int c = c0; c < c1; ++c) n += order_key(__bfloat16_as_ushort(row[c])) == (uint32_t)kr;
+    int tot;
+    const int base = block_exclusive_scan(n, sm.warp_sums, &tot);
+    if (tid == 0) sm.found = 0;
+    __syncthreads();
+    if (kr >= 0 && base <= jr && jr < base + n) {
+        int k = base;
+        for (int c = c0; c < c1; ++c) {
+            if (order_key(__bfloat16_as_ushort(row[c])) == (uint32_t)kr) {
+                if (k == jr) {
+                    sm.found = c;
+                    break;
+                }
+                ++k;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) out[blockIdx.x] = sm.found;
+}
+
 __global__ void __launch_bounds__(kSampleThreads)
     sample_rows_kernel(int* __restrict__ out, const bf16* __restrict__ logits, int vocab,
                        float temperature, int top_k, float top_p,
@@ -464,11 +705,28 @@ int nc_sample_rows(int* out, const void* logits, int rows, int vocab, float temp
     if (reinterpret_cast<uintptr_t>(logits) & 15) return NC_ERR_MISALIGNED;
     if (temperature == 0.f) return nc_argmax_rows(out, logits, rows, vocab, stream);
     if (!(top_p > 0.f) || !uniforms) return NC_ERR_INVALID_ARG;
-    // top_k <= 0 or >= vocab: no top-k filter.  Then top_p must be off (>= 1): a top-p cut over
-    // the whole vocabulary (a full sort) is not supported.
+    // top_k <= 0 or >= vocab: no top-k filter (top_p, if on, then cuts the whole row; its
+    // per-key counters are 16-bit, which holds for vocab <= 65536).
     const bool no_topk = top_k <= 0 || top_k >= vocab;
-    if (no_topk && top_p < 1.0f) return NC_ERR_INVALID_ARG;
     if (!no_topk && top_k > kSampleMaxK) return NC_ERR_INVALID_ARG;
+    if (no_topk && top_p < 1.0f) {
+        if (vocab > 65536) return NC_ERR_INVALID_ARG;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return internal_cuda_fail(e);
+        if (dev < 0 || dev >= kTopPMaxDev) return NC_ERR_INVALID_ARG;
+        static bool attr_set[kTopPMaxDev] = {};
+        if (!attr_set[dev]) {
+            e = cudaFuncSetAttribute(sample_top_p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kTopPCountBytes);
+            if (e != cudaSuccess) return internal_cuda_fail(e);
+            attr_set[dev] = true;
+        }
+        sample_top_p_kernel<<<rows, kSampleThreads, kTopPCountBytes, stream>>>(
+            out, static_cast<const bf16*>(logits), vocab, temperature, top_p, uniforms);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? NC_OK : internal_cuda_fail(e);
+    }
     if (no_topk) top_k = 0;
     sample_rows_kernel<<<rows, kSampleThreads, 0, stream>>>(
         out, static_cast<const bf16*>(logits), vocab, temperature, top_k, top_p, uniforms);

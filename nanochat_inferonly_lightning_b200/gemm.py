@@ -104,8 +104,9 @@ def argmax_rows(out, logits, stream=None):
 
 def sample_rows(out, logits, temperature, top_k, top_p, uniforms, stream=None):
     """Engine::sample (src/engine.cpp:62-131) on the device: out[r] (int32) drawn from
-    logits[r] (bf16 [rows, vocab]) with temperature, top-k (1..1024) and top-p, using the
-    uniform draw uniforms[r] (float32 CUDA tensor [rows]); temperature 0 is greedy."""
+    logits[r] (bf16 [rows, vocab]) with temperature, top-k (1..1024; 0 or >= vocab: off) and
+    top-p (>= 1: off; with top-k off it cuts the whole row), using the uniform draw uniforms[r]
+    (float32 CUDA tensor [rows]); temperature 0 is greedy."""
     _bf16(logits)
     if out.dtype != torch.int32:
         raise TypeError(f"out must be int32, got {out.dtype}")

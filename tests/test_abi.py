@@ -150,8 +150,9 @@ def test_step_ops_argument_validation_without_gpu():
     assert lib.nc_argmax_rows(P(256), P(264), 4, 65536, None) == 2
     assert lib.nc_argmax_rows(P(256), P(256), 0, 65536, None) == 0
     F = ctypes.c_float
-    # sampling: top_k above 1024 with a filter, or top-p over the whole vocabulary, is refused
+    # sampling: top_k above 1024 with a filter, top_p <= 0, no draws or a negative temperature
+    # are refused
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 2000, F(0.9), P(256), None) == 1
-    assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 0, F(0.9), P(256), None) == 1
+    assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 0, F(0.0), P(256), None) == 1
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 50, F(0.9), None, None) == 1
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(-1.0), 50, F(0.9), P(256), None) == 1

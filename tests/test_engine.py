@@ -126,6 +126,30 @@ def test_sampled_decode_in_graph(setup):
     assert torch.equal(runs[0], runs[1])
 
 
+def test_top_p_only_sampling_in_graph(setup):
+    """top_k off and top_p 0.9 (Engine::top_p_filter over the whole vocabulary) inside the
+    captured step: every sampled token lies in its row's nucleus (exact sums over the row sorted
+    by descending probability, 1e-4 slack at the edge), and two engines seeded alike sample the
+    same tokens."""
+    nc, E, w, prompts = setup
+    runs = []
+    for _ in range(2):
+        eng = E.BatchedEngine(w, B, MAX_LEN, temperature=0.8, top_k=0, top_p=0.9, seed=7)
+        eng.prefill(prompts)
+        toks = [eng.capture()]
+        for _ in range(3):
+            t = eng.step().clone()
+            pr = torch.softmax(eng.logits.double() / 0.8, dim=-1)
+            for s in range(B):
+                srt, idx = torch.sort(pr[s], descending=True, stable=True)
+                cs = torch.cumsum(srt, 0)
+                pos = int((idx == int(t[s])).nonzero()[0, 0])
+                assert pos == 0 or float(cs[pos - 1]) <= 0.9 + 1e-4, (s, pos)
+            toks.append(t)
+        runs.append(torch.stack(toks))
+    assert torch.equal(runs[0], runs[1])
+
+
 def test_continuous_batching(setup):
     """Sequences join and leave the running batch between graph replays (admit / retire)
     without re-capturing: a sequence admitted into slot 2 after three steps of slot 0 produces

@@ -287,7 +287,9 @@ def _sample_margin(row_f32, T, k, p, r):
     pr /= pr.sum()
     if 0 < k < len(pr):
         order = np.lexsort((np.arange(len(pr)), -pr))[:k]
-    else:  # no top-k filter: index order
+    elif p < 1.0:  # top-p alone sorts the whole row
+        order = np.lexsort((np.arange(len(pr)), -pr))
+    else:  # no filter: index order
         order = np.arange(len(pr))
     cs = np.cumsum(pr[order])
     m = np.abs(cs - p).min() if p < 1.0 else 1.0
@@ -342,6 +344,39 @@ def test_sample_rows_against_oracle(G):
             cs = np.cumsum(w / w.sum())
             lo = cs[got[r] - 1] if got[r] > 0 else 0.0
             assert lo - 1e-4 <= uh[r] <= cs[got[r]] + 1e-4, (T, k, r, got[r])
+    # top-p over the whole row (top_k off).  The kept prefix can hold thousands of entries with
+    # intervals ~1e-5 wide, so the check is against exact (fp64) sums over the row sorted as
+    # the reference sorts it (descending probability, ties by ascending index): the chosen index
+    # must lie in the prefix whose running sum first exceeds top_p (within 1e-4 of the edge),
+    # and its renormalised interval must lie within 1e-4 of r.  Rows where the peaked
+    # distribution leaves wide intervals must give the oracle's token exactly.  Row 7 is made
+    # constant: all 65536 entries share one key (the case a 16-bit per-key count cannot hold).
+    lg = logits.clone()
+    lg[7] = 1.5
+    host_p = oracle.f32_to_bf16_bits(lg.float().cpu().numpy())
+    exact_rows = 0
+    for T, k, p in [(1.0, 0, 0.9), (0.6, 0, 0.5), (2.0, V, 0.95), (0.3, 0, 0.99)]:
+        out = torch.empty(R, dtype=torch.int32, device="cuda")
+        G.sample_rows(out, lg, T, k, p, u)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for r in range(R):
+            lf = oracle.bf16_bits_to_f32(host_p[r]).astype(np.float64)
+            pr = np.exp((lf - lf.max()) / T)
+            pr /= pr.sum()
+            order = np.lexsort((np.arange(V), -pr))
+            cs = np.cumsum(pr[order])
+            pos = int(np.nonzero(order == got[r])[0][0])
+            cut = int(np.argmax(cs > p)) + 1 if (cs > p).any() else V
+            assert pos < cut or cs[pos - 1] <= p + 1e-4, (T, k, p, r, pos, cut)
+            s2 = cs[cut - 1]
+            lo = cs[pos - 1] / s2 if pos > 0 else 0.0
+            hi = cs[pos] / s2
+            assert lo - 1e-4 <= uh[r] <= hi + 1e-4, (T, k, p, r, got[r], lo, hi, uh[r])
+            if _sample_margin(oracle.bf16_bits_to_f32(host_p[r]), T, k, p, float(uh[r])) > 1e-4:
+                assert got[r] == oracle.sample(host_p[r], T, k, p, float(uh[r])), (T, k, p, r)
+                exact_rows += 1
+    assert exact_rows >= R // 2, exact_rows
     # temperature 0 is the greedy path
     out = torch.empty(R, dtype=torch.int32, device="cuda")
     G.sample_rows(out, logits, 0.0, 50, 0.9, None)
