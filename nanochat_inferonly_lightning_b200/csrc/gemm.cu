@@ -841,13 +841,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 rs = tail->rs[quarter * 32 + lane];
                 __syncwarp();
             }
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait_cl(&tail->acc_full[buf], (lt >> 1) & 1,
-                                                      abort_flag, p.status, kTagPAccFull)))
-                break;
-            tc_fence_after();
-            // The residual of the first chunk, then each next chunk's ahead of this one's work:
-            // its loads are in flight while this chunk is read from TMEM and stored.
-            uint4 rnext[4];
             auto load_res = [&](int c, uint4 (&r)[4]) {
 #pragma unroll
                 for (int g8 = 0; g8 < 4; ++g8) {
@@ -857,12 +850,24 @@ __global__ void __launch_bounds__(kTThreads, 1)
                                 : make_uint4(0u, 0u, 0u, 0u);
                 }
             };
-            load_res(0, rnext);
-            for (int c = 0; c < kTBN / 32; ++c) {
-                uint4 rcur[4];
+            // With a residual known at compile time, this thread's whole residual row segment
+            // (8 chunks x 32 columns, 128 registers) is loaded before the accumulator wait, so
+            // its latency hides behind the tile's MMAs.  The residual is an input of the kernel
+            // (read after griddepcontrol.wait) and each element is read and then written by the
+            // one thread that owns it, so the early loads are safe when out == residual.
+            constexpr bool kPreload = KF >= 0 && (KF & NC_GEMM_RESIDUAL) != 0;
+            uint4 rall[kPreload ? kTBN / 32 : 1][4];
+            if constexpr (kPreload) {
 #pragma unroll
-                for (int g8 = 0; g8 < 4; ++g8) rcur[g8] = rnext[g8];
-                if (c + 1 < kTBN / 32) load_res(c + 1, rnext);
+                for (int c = 0; c < kTBN / 32; ++c) load_res(c, rall[c]);
+            }
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_cl(&tail->acc_full[buf], (lt >> 1) & 1,
+                                                      abort_flag, p.status, kTagPAccFull)))
+                break;
+            tc_fence_after();
+            // One 32-column chunk: read it from TMEM (the last chunk also frees the buffer),
+            // apply the fused steps and store.
+            auto do_chunk = [&](int c, const uint4 (&rcur)[4]) {
                 uint32_t v[32];
                 tmem_ld32_sync(tmem + buf * kTBN + 32 * c + lane_base, v);
                 if (c == kTBN / 32 - 1) {
@@ -873,7 +878,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     if (lane == 0)
                         mbar_arrive_cluster(map_shared_rank_u32(smem_u32(&tail->acc_empty[buf]), 0));
                 }
-                if (m >= p.M) continue;
+                if (m >= p.M) return;
 #pragma unroll
                 for (int g8 = 0; g8 < 4; ++g8) {
                     const int n = n0 + 32 * c + 8 * g8;
@@ -906,6 +911,22 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     bf16* dst = p.out + (size_t)(n / seg) * ((size_t)p.M * seg) + (size_t)m * seg +
                                 (n % seg);
                     *reinterpret_cast<uint4*>(dst) = f32_to_bf16x8(f);
+                }
+            };
+            if constexpr (kPreload) {
+#pragma unroll
+                for (int c = 0; c < kTBN / 32; ++c) do_chunk(c, rall[c]);
+            } else {
+                // The residual of the first chunk, then each next chunk's ahead of this one's
+                // work: its loads are in flight while this chunk is read from TMEM and stored.
+                uint4 rnext[4];
+                load_res(0, rnext);
+                for (int c = 0; c < kTBN / 32; ++c) {
+                    uint4 rcur[4];
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) rcur[g8] = rnext[g8];
+                    if (c + 1 < kTBN / 32) load_res(c + 1, rnext);
+                    do_chunk(c, rcur);
                 }
             }
         }
