@@ -323,9 +323,9 @@ int nc_argmax_rows(int* out, const void* logits, int rows, int cols, cudaStream_
  * reference draws them from its mt19937).  With neither filter the row is sampled in index
  * order.  Equal probabilities are taken in ascending index order (the reference's sort leaves
  * their order unspecified).  With top-k, the top-p cut, the renormalisation and the running
- * sums are the reference's sequential fp32 sums; top-p over the whole row (top_k off) finds the
- * cut and the draw from exact sums of the probabilities, without a sort; the softmax
- * denominator is a parallel fp32 sum. */
+ * sums are the reference's sequential fp32 sums; top-p over the whole row (top_k off; vocab <=
+ * 65536, else NC_ERR_INVALID_ARG) finds the cut and the draw from exact sums of the
+ * probabilities, without a sort; the softmax denominator is a parallel fp32 sum. */
 int nc_sample_rows(int* out, const void* logits, int rows, int vocab, float temperature,
                    int top_k, float top_p, const float* uniforms, cudaStream_t stream);
 

@@ -154,5 +154,7 @@ def test_step_ops_argument_validation_without_gpu():
     # are refused
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 2000, F(0.9), P(256), None) == 1
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 0, F(0.0), P(256), None) == 1
+    # top-p over the whole row counts keys in 16 bits: vocab above 65536 is refused
+    assert lib.nc_sample_rows(P(256), P(256), 4, 65544, F(1.0), 0, F(0.9), P(256), None) == 1
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(1.0), 50, F(0.9), None, None) == 1
     assert lib.nc_sample_rows(P(256), P(256), 4, 65536, F(-1.0), 50, F(0.9), P(256), None) == 1
