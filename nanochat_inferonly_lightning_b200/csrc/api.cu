@@ -205,7 +205,7 @@ int decode_common(void* out, const void* q, const void* k_new, const void* v_new
     const bool head_layout = decode_use_head_layout(batch, max_kv_len, split_len);
     // Splits combined through a global workspace: all but the per-head layout's cluster case.
     const bool uses_ws =
-        max_splits > 1 && !(head_layout && decode_head_cluster(max_splits, overlap != 0));
+        max_splits > 1 && !(head_layout && decode_head_cluster(max_splits, batch, overlap != 0));
     if (uses_ws && (!ws || ws_bytes < need)) return NC_ERR_WORKSPACE;
     DecodeArgs a{};
     if (k_new) {
@@ -334,7 +334,7 @@ int flash_attention_impl(void* out, const void* Q, const void* K, const void* V,
         const int T = auto_split_len(1, std::max(n_visible, 1));
         const int splits = std::max(1, (std::max(n_visible, 0) + T - 1) / T);
         if (splits > 1 && !(decode_use_head_layout(1, std::max(n_visible, 0), 0) &&
-                            decode_head_cluster(splits, false))) {
+                            decode_head_cluster(splits, 1, false))) {
             int st = single_ws(heads, std::max(n_visible, 0), stream, &ws, &wsb);
             if (st) return st;
         }

@@ -940,7 +940,7 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
         // overlapped launch: its CTAs start beside the still-running GEMM, which a cluster,
         // placed whole inside one GPC, would hold back (measured: the engine's decode step
         // 1.69 ms with clusters against 1.50 without).
-        const bool cluster = decode_head_cluster(a.max_splits, a.overlap != 0);
+        const bool cluster = decode_head_cluster(a.max_splits, a.batch, a.overlap != 0);
         static bool cl_attr[64] = {};
         if (cluster && !cl_attr[dev]) {
             for (auto fn : {decode_head_kernel<false, true>, decode_head_kernel<true, true>}) {
