@@ -115,9 +115,10 @@ int auto_split_len(int batch, int max_kv_len) {
         }
     }
     long long t = best_t;
-    // A small batch that is too long for the per-head layout: longer splits, fewer partials to
-    // combine (measured: 8 sequences x 1024 keys, 23.7 us with 80-key splits, 26.8 with 32).
-    if (batch <= kDecodeHeadMaxBatch) t = std::max<long long>(t, 80);
+    // A batch of at most 8 that is too long for the per-head layout: longer splits, fewer
+    // partials to combine (measured: 8 sequences x 1024 keys, 23.7 us with 80-key splits, 26.8
+    // with 32).
+    if (batch <= 8) t = std::max<long long>(t, 80);
     t = (t + 15) / 16 * 16;
     return (int)std::min<long long>(std::max<long long>(t, 16), 1024);
 }

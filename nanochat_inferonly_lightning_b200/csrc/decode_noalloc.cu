@@ -97,7 +97,8 @@ extern "C" int nc_decode_attention_noalloc(void* out, const void* q, const void*
     // Split plan: the one nc_decode_attention makes for these sizes (same split length, same
     // layout), with the split length doubled only while the partial results would not fit in
     // the array (a single split needs no partials at all).  The per-head layout's calls
-    // (<= 8 sequences, <= 8192 keys in all) always fit: at most 128 splits x 31 heads.
+    // (<= 16 sequences, <= 16384 keys in all, 64-key splits) always fit: at most 256
+    // (sequence, split) pairs x 31 heads x 520 bytes.
     const int L = std::max(max_kv_len, 1);
     const int T_auto = internal_auto_split_len(batch, L);
     long long T = T_auto;

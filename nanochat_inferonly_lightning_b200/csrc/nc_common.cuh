@@ -243,9 +243,12 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
 // and, with automatic splits, at most kDecodeHeadMaxKeys keys in total (batch * max_kv_len).
 // With the cache rows staged in shared memory (six CTAs per SM), measured at 8 sequences of
 // cfg3's lengths (longest ~2048): 22.1 / 18.5 / 26.7 us against 24.7 / 22.3 / 29.1 for the
-// streaming layout, and at 8 x 4096 keys 65.3 against 59.6, so the bound is 8 x 2048.  An
-// explicit split length above kDecodeHeadSplit selects the streaming layout.
-constexpr int kDecodeHeadMaxBatch = 8;
+// streaming layout, and at 8 x 4096 keys 65.3 against 59.6, so the bound is 8 x 2048.  Up to
+// 16 sequences: cfg3's 8-way shards of 9-10 sequences take 22.7-22.9 us against 25.7-26.0 on
+// the streaming layout, 12 x 1024 keys 29.0 against 35.1, 16 x 300 17.2 against 18.7 (evenly
+// long 9-12 sequences of 600-850 keys lose 0.7-1.6 us).  An explicit split length above
+// kDecodeHeadSplit selects the streaming layout.
+constexpr int kDecodeHeadMaxBatch = 16;
 constexpr int kDecodeHeadSplit = 64;
 constexpr long long kDecodeHeadMaxKeys = 16384;
 inline bool decode_use_head_layout(int batch, int max_kv_len, int split_len) {

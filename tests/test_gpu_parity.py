@@ -316,6 +316,12 @@ def test_decode_batched_unfused(nc):
     _decode_batch(nc, [3, 64, 65, 700], 0, seed=400, fused=False)
 
 
+def test_decode_batched_head_layout_many_sequences(nc):
+    """Up to 16 sequences and 16384 keys in all take the per-head layout: 12 ragged sequences,
+    the longest with 21 splits (global combine) and the shortest with one."""
+    _decode_batch(nc, [1, 40, 64, 65, 200, 333, 512, 700, 900, 1100, 1250, 1300], 0, seed=430)
+
+
 def test_decode_batched_streaming_layout(nc):
     """More than 8 sequences: the streaming layout (all heads of a split per work item, CTAs
     taking items from a queue), with automatic splits."""
@@ -327,7 +333,7 @@ def test_decode_batched_streaming_layout(nc):
     ([300, 7, 64, 65], 16, H, 0),                     # per-head layout, small pages
     ([1, 5, 16, 33, 64, 128, 300, 511, 777, 1024, 1500, 2047], 48, H, 0),  # streaming
     ([40, 700, 1300], 128, H, 80),                    # streaming, explicit split
-    ([3, 90, 250, 600, 1000, 11, 77, 500, 333], 16, 20, 0),  # streaming, 6-row stages
+    ([3, 90, 250, 600, 1000, 11, 77, 500, 333], 16, 20, 80),  # streaming, 6-row stages
 ])
 def test_decode_paged(nc, lens, page_rows, heads, split_len):
     """nc_decode_attention_paged: K/V rows live in shuffled pages of two pools; the new key and
