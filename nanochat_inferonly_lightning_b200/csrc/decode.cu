@@ -732,7 +732,8 @@ __global__ void __launch_bounds__(128, 6) decode_head_kernel(DecodeArgs a) {
         cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
         cluster.sync();  // release / acquire: every split's partial is visible
         if (split == 0 && warp == 0) {
-            // The same arithmetic, in the same split order, as the global combine below.
+            // The same arithmetic, in the same split order, as the global combine of up to 8
+            // splits below.
             float2 ml[16];
             float4 v[16];
 #pragma unroll
@@ -765,45 +766,53 @@ __global__ void __launch_bounds__(128, 6) decode_head_kernel(DecodeArgs a) {
         cluster.sync();  // no CTA leaves while CTA 0 still reads its shared memory
         return;
     }
-    if (warp != 0) return;
-    // Warp 0: lane owns dims [4*lane, 4*lane+4).
-    float M = kNegInf;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w].x);
-    const float mu = (M == kNegInf) ? 0.f : M;
-    float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const float wt = fast_exp2(sm_ml[w].x - mu);
-        den = __fmaf_rn(sm_ml[w].y, wt, den);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o4[i] = __fmaf_rn(sm_o[w][4 * lane + i], wt, o4[i]);
-    }
-    if (n_splits == 1) {
-        const float inv = 1.0f / den;
-        uint2 r;
-        r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
-        r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
-        *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
-        return;
-    }
-    // Partial result of this split (max, sum, unnormalised output), then the ticket.
-    const size_t pidx = ((size_t)b * a.max_splits + split) * H + h;
-    __stcg(reinterpret_cast<float4*>(a.part_o + pidx * kHeadDim) + lane,
-           make_float4(o4[0], o4[1], o4[2], o4[3]));
-    if (lane == 0) __stcg(a.part_ml + pidx, make_float2(M, den));
-    __threadfence();
-    __syncwarp();
-    unsigned ticket = 0;
+    // Warp 0 merges the four warps into this split's (max, sum, output) and, with several
+    // splits, stores it and takes the ticket of its (sequence, head).  The other warps wait
+    // for the outcome: above 8 splits the last split's combine is shared by all four warps.
+    __shared__ int sm_last;
     unsigned* ctr = a.counters + kQueueWords + (size_t)b * H + h;
-    if (lane == 0) ticket = atomicAdd(ctr, 1u);
-    ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
-    if (ticket != (unsigned)(n_splits - 1)) return;
-    // Last split of (b, h): combine.
+    if (warp == 0) {
+        // Warp 0: lane owns dims [4*lane, 4*lane+4).
+        float M = kNegInf;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w].x);
+        const float mu = (M == kNegInf) ? 0.f : M;
+        float den = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float wt = fast_exp2(sm_ml[w].x - mu);
+            den = __fmaf_rn(sm_ml[w].y, wt, den);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o4[i] = __fmaf_rn(sm_o[w][4 * lane + i], wt, o4[i]);
+        }
+        if (n_splits == 1) {
+            const float inv = 1.0f / den;
+            uint2 r;
+            r.x = pack_bf16x2(o4[0] * inv, o4[1] * inv);
+            r.y = pack_bf16x2(o4[2] * inv, o4[3] * inv);
+            *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
+        } else {
+            // Partial result of this split (max, sum, unnormalised output), then the ticket.
+            const size_t pidx = ((size_t)b * a.max_splits + split) * H + h;
+            __stcg(reinterpret_cast<float4*>(a.part_o + pidx * kHeadDim) + lane,
+                   make_float4(o4[0], o4[1], o4[2], o4[3]));
+            if (lane == 0) __stcg(a.part_ml + pidx, make_float2(M, den));
+            __threadfence();
+            __syncwarp();
+            unsigned ticket = 0;
+            if (lane == 0) ticket = atomicAdd(ctr, 1u);
+            ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+            if (lane == 0) sm_last = ticket == (unsigned)(n_splits - 1) ? 1 : 0;
+        }
+    }
+    if (n_splits == 1) return;  // uniform across the CTA
+    __syncthreads();            // sm_last written; warp 0 has read sm_o / sm_ml
+    if (!sm_last) return;       // uniform: only the last split of (b, h) combines
     __threadfence();
-    if (lane == 0) *ctr = 0u;  // ready for the next launch
+    if (threadIdx.x == 0) *ctr = 0u;  // ready for the next launch
     const size_t base = (size_t)b * a.max_splits * H + h;
     if (n_splits <= 8) {
+        if (warp != 0) return;
         // Up to 8 splits (up to 512 keys): every partial is loaded in one round trip.
         float4 v[8];
         float2 ml[8];
@@ -836,50 +845,65 @@ __global__ void __launch_bounds__(128, 6) decode_head_kernel(DecodeArgs a) {
         *reinterpret_cast<uint2*>(out_row + 4 * lane) = rf;
         return;
     }
-    float2 ml0 = make_float2(kNegInf, 0.f);
-    if (lane < n_splits) ml0 = __ldcg(a.part_ml + base + (size_t)lane * H);
-    float Mc = ml0.x;
-    for (int sp = lane + 32; sp < n_splits; sp += 32)
-        Mc = fmaxf(Mc, __ldcg(a.part_ml + base + (size_t)sp * H).x);
+    // More than 8 splits: warp w combines splits w, w + 4, w + 8, ... , four per round trip
+    // (two round trips for up to 32 splits), merged online, then warp 0 merges the
+    // four warps' results.  Lane owns dims [4*lane, 4*lane+4).
+    {
+        float Mw = kNegInf, dw = 0.f, ow[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = warp; c0 < n_splits; c0 += 16) {
+            float4 v[4];
+            float2 ml[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xFFFFFFFFu, Mc, o));
-    const float muc = (Mc == kNegInf) ? 0.f : Mc;
-    float dc = 0.f, oc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int g0 = 0; g0 < n_splits; g0 += 32) {
-        float2 ml = ml0;
-        if (g0 > 0)
-            ml = g0 + lane < n_splits ? __ldcg(a.part_ml + base + (size_t)(g0 + lane) * H)
-                                      : make_float2(kNegInf, 0.f);
-        const float w = fast_exp2(ml.x - muc);
-        float lw = ml.y * w;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, o);
-        dc += lw;
-        const int cnt = min(32, n_splits - g0);
-        for (int sp0 = 0; sp0 < cnt; sp0 += 8) {
-            float4 v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int sp = sp0 + i;
-                v[i] = sp < cnt ? __ldcg(reinterpret_cast<const float4*>(
-                                      a.part_o + (base + (size_t)(g0 + sp) * H) * kHeadDim) + lane)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < 4; ++i) {
+                const int sp = c0 + 4 * i;
+                const bool ok = sp < n_splits;
+                v[i] = ok ? __ldcg(reinterpret_cast<const float4*>(
+                                a.part_o + (base + (size_t)sp * H) * kHeadDim) + lane)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                ml[i] = ok ? __ldcg(a.part_ml + base + (size_t)sp * H) : make_float2(kNegInf, 0.f);
             }
+            float Mc = kNegInf;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float wi = __shfl_sync(0xFFFFFFFFu, w, (sp0 + i) & 31);
-                oc[0] = __fmaf_rn(v[i].x, wi, oc[0]);
-                oc[1] = __fmaf_rn(v[i].y, wi, oc[1]);
-                oc[2] = __fmaf_rn(v[i].z, wi, oc[2]);
-                oc[3] = __fmaf_rn(v[i].w, wi, oc[3]);
+            for (int i = 0; i < 4; ++i) Mc = fmaxf(Mc, ml[i].x);
+            const float Mn = fmaxf(Mw, Mc);
+            const float mun = (Mn == kNegInf) ? 0.f : Mn;
+            const float sc = fast_exp2(Mw - mun);  // 0 while nothing is merged (Mw = -inf)
+            dw *= sc;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ow[k] *= sc;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float w = fast_exp2(ml[i].x - mun);
+                dw = __fmaf_rn(ml[i].y, w, dw);
+                ow[0] = __fmaf_rn(v[i].x, w, ow[0]);
+                ow[1] = __fmaf_rn(v[i].y, w, ow[1]);
+                ow[2] = __fmaf_rn(v[i].z, w, ow[2]);
+                ow[3] = __fmaf_rn(v[i].w, w, ow[3]);
             }
+            Mw = Mn;
         }
+        if (lane == 0) sm_ml[warp] = make_float2(Mw, dw);
+        *reinterpret_cast<float4*>(&sm_o[warp][4 * lane]) = make_float4(ow[0], ow[1], ow[2], ow[3]);
     }
-    const float inv = 1.0f / dc;
-    uint2 r;
-    r.x = pack_bf16x2(oc[0] * inv, oc[1] * inv);
-    r.y = pack_bf16x2(oc[2] * inv, oc[3] * inv);
-    *reinterpret_cast<uint2*>(out_row + 4 * lane) = r;
+    __syncthreads();
+    if (warp != 0) return;
+    float Mf = kNegInf;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) Mf = fmaxf(Mf, sm_ml[w].x);
+    const float muf = (Mf == kNegInf) ? 0.f : Mf;
+    float df = 0.f, of[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float wt = fast_exp2(sm_ml[w].x - muf);
+        df = __fmaf_rn(sm_ml[w].y, wt, df);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) of[i] = __fmaf_rn(sm_o[w][4 * lane + i], wt, of[i]);
+    }
+    const float invf = 1.0f / df;
+    uint2 rf;
+    rf.x = pack_bf16x2(of[0] * invf, of[1] * invf);
+    rf.y = pack_bf16x2(of[2] * invf, of[3] * invf);
+    *reinterpret_cast<uint2*>(out_row + 4 * lane) = rf;
 }
 
 }  // namespace
