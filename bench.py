@@ -780,12 +780,14 @@ def bench_chunked(impl, dist, stepper, K, Wm, peaks, traffic):
             offs = torch.full((n,), off, dtype=torch.int32, device="cuda")
 
             def step():
+                # one RoPE/QK-norm/append launch for the whole batch of chunks, then one
+                # attention launch over it (the reference arm has no batched entry points)
                 q, k, v, kslab, vslab, out = sets[it[0] % R]
                 it[0] += 1
-                for i in range(n):
-                    st = lib.nc_rope_qknorm_append(ptr(q[i]), ptr(k[i]), ptr(v[i]), ptr(kslab[i]),
-                                                   ptr(vslab[i]), C, H, off, stream())
-                    assert st == 0, st
+                st = lib.nc_rope_qknorm_append_batched(ptr(q), ptr(k), ptr(v), ptr(kslab),
+                                                       ptr(vslab), rows * ROW, n, C, H, off,
+                                                       stream())
+                assert st == 0, st
                 st = lib.nc_prefill_attention_batched(ptr(out), ptr(q), ptr(kslab), ptr(vslab),
                                                       rows * ROW, rows, ptr(offs), n, C, H,
                                                       W.SCALE, stream())
