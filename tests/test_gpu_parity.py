@@ -401,14 +401,17 @@ def test_decode_paged_bad_page_id_is_flagged(nc):
     assert int(kpool[2, 39 % 16].count_nonzero()) > 0 and int(kpool[7, 49 % 16].count_nonzero()) > 0
 
 
-def test_decode_overlap_after_qkv_gemm(nc):
+@pytest.mark.parametrize("lens", [
+    [257, 300, 333, 401, 450, 479, 505, 520],                       # the engine's 8 sequences
+    [64, 129, 300, 450, 520, 700, 800, 950, 1000, 1100, 1200, 1300],  # 12: up to 21 splits
+])
+def test_decode_overlap_after_qkv_gemm(nc, lens):
     """nc_decode_attention_overlap right after the fused Q/K/V GEMM that produces its q, k_new
     and v_new (the engine's order): the attention CTAs load cache rows while the GEMM runs and
     wait for it before reading q/k/v.  Same bits as the plain call made after a synchronize, and
-    the oracle's result for the GEMM's q/k/v.  Eight sequences of up to 520 keys: the per-head
-    layout."""
-    lens = [257, 300, 333, 401, 450, 479, 505, 520]
-    B, max_len = len(lens), 520
+    the oracle's result for the GEMM's q/k/v.  Both cases take the per-head layout (up to 16
+    sequences and 16384 keys); the second combines more than 8 splits per head."""
+    B, max_len = len(lens), max(lens)
     g = torch.Generator(device="cuda").manual_seed(610)
     x = torch.randn((B, H * D), generator=g, device="cuda").to(torch.bfloat16)
     w = (torch.randn((3 * H * D, H * D), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
